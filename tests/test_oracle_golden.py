@@ -1,0 +1,205 @@
+"""Pin the CPU oracle to the reference's own test oracles and known answers (no GPU).
+
+Golden vectors come from tests/golden/make_golden.py, an independent numpy restatement of
+the reference's in-test CPU oracles; the cases below mirror the reference tests named in
+each docstring.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as o
+
+
+def _logical(codes, width, bits):
+    return codes[:, : width // (32 // bits)]
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("width", [256, 768, 1280, 5120, 6144, 8192, 17408])
+def test_rotated_packing_matches_golden(golden, bits, width):
+    """src/quantized.rs:1072-1129 rotated_packing_cpu_oracle: exact codes, scales 1e-6."""
+    key = f"pack_b{bits}_w{width}"
+    x = golden[key + "_x"]
+    stride = width + 512 // bits
+    storage, codes, scales, _ = o.prepare(x, bits, stride)
+    assert np.array_equal(_logical(codes, width, bits), golden[key + "_words"])
+    exp = golden[key + "_scales"]
+    assert np.all(np.abs(scales - exp) <= exp * 1e-6)
+    # storage layout: codes[rows][stride/P] then f32 scales (src/quantized.rs:656-664)
+    words = stride // (32 // bits)
+    assert storage.size == 3 * (words + 1)
+    assert np.array_equal(storage[3 * words:].view(np.float32), scales)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_exceptional_rows_match_golden(golden, bits):
+    """src/quantized.rs:1131-1185: NaN / Inf / bf16 MAX rows get an inf scale and zero codes;
+    subnormal rows keep the 1e-30 floor."""
+    x = golden[f"exc_b{bits}_x"]
+    _, codes, scales, _ = o.prepare(x, bits, 5120 + 512 // bits)
+    assert np.array_equal(_logical(codes, 5120, bits), golden[f"exc_b{bits}_words"])
+    assert np.array_equal(scales.view(np.uint32), golden[f"exc_b{bits}_scales"].view(np.uint32))
+    assert np.isinf(scales[3]) and np.isinf(scales[4]) and np.isinf(scales[5])
+    assert not np.any(_logical(codes, 5120, bits)[3:6])
+
+
+def test_rotation_preserves_inner_product():
+    """src/quantized.rs:857-876: <Ha, Hb>/256 == <a, b> within 1e-8 (f64 sums)."""
+    i = np.arange(512)
+    a = o.f32_to_bf16(((i * 17 % 71).astype(np.float32) - 35) / 64)
+    b = o.f32_to_bf16(((i * 31 % 59).astype(np.float32) - 29) / 64)
+    expected = float(np.dot(o.bf16_to_f32(a).astype(np.float64), o.bf16_to_f32(b).astype(np.float64)))
+    # Recover the rotation from prepare: with 8-bit codes the rotated values are the codes
+    # scaled back, too coarse here; so compare through the golden numpy rotation instead.
+    from tests.golden.make_golden import rotated
+    actual = float(np.dot(rotated(a).astype(np.float64), rotated(b).astype(np.float64)) / 256)
+    assert abs(actual - expected) < 1e-8
+
+
+@pytest.mark.parametrize("bits,rows,cols,padded", [(4, 256, 1024, True), (4, 384, 512, False),
+                                                  (8, 128, 256, False)])
+def test_retile_block_formula(bits, rows, cols, padded):
+    """src/quantized.rs:1369-1407 retiled_codes_match_block_formula."""
+    stride = cols + (512 // bits if padded else 0)
+    in_words, words = stride // (32 // bits), cols // (32 // bits)
+    values = (np.arange(rows * in_words, dtype=np.uint64) * 2654435761 % (1 << 32)).astype(np.uint32)
+    tiled = o.retile(values.reshape(rows, in_words), rows, cols, bits)
+    assert tiled.size == rows * words
+    n, q = np.meshgrid(np.arange(rows), np.arange(words), indexing="ij")
+    at = ((n // 128) * (words // 32) + q // 32) * 4096 + (n % 128) * 32 + q % 32
+    assert np.array_equal(tiled[at], values.reshape(rows, in_words)[:, :words])
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("index", [0, 1])
+@pytest.mark.parametrize("rows", [1, 17])
+@pytest.mark.parametrize("start", [0, 1])
+def test_gemm_matches_integer_dot(golden, bits, index, rows, start):
+    """src/quantized.rs:977-1070: int32 accumulators exact; bf16 output within
+    max(|a|,|e|)/128 + 1e-6 of bf16(dot * a_scale * w_scale)."""
+    key = f"gemm_b{bits}_i{index}_r{rows}_s{start}"
+    w = golden[f"gemm_b{bits}_i{index}_w"]
+    wt, ws = o.pack_weight(w, bits)
+    _, codes, scales, _ = o.prepare(golden[key + "_x"], bits, 256)
+    out, acc = o.gemm(codes, scales, wt, ws, 256, 256, bits=bits, want_acc=True)
+    assert np.array_equal(acc, golden[key + "_dot"])
+    actual = o.bf16_to_f32(out)
+    expected = golden[key + "_expected"]
+    assert np.all(np.isfinite(actual))
+    tol = np.maximum(np.abs(actual), np.abs(expected)) / 128 + 1e-6
+    assert np.all(np.abs(actual - expected) <= tol)
+
+
+@pytest.mark.parametrize("experts,topk", [(128, 8), (64, 8), (128, 4)])
+@pytest.mark.parametrize("phase", [0, 1, 2, 3])
+@pytest.mark.parametrize("bf", [0, 1])
+def test_router_matches_serial_spec(golden, experts, topk, phase, bf):
+    """src/benchmarking/omni.rs:6-102: ids equal the serial scan exactly (ties and +-0 go
+    to the lowest id); probabilities within one bf16 step (exp bits are unpinned)."""
+    key = f"route_e{experts}_k{topk}_p{phase}_bf{bf}"
+    routes = o.route(golden[key + "_logits"], topk)
+    assert np.array_equal(routes[:, :topk], golden[key + "_ids"])
+    p, e = routes[:, topk:], golden[key + "_probs"]
+    assert np.all(np.abs(p - e) <= np.maximum(np.abs(e), 1e-30) / 128)
+
+
+@pytest.mark.parametrize("tokens", [1, 17, 64, 65, 128, 255, 256])
+@pytest.mark.parametrize("phase", [0, 1, 2])
+def test_grouping_order_tasks(golden, tokens, phase):
+    """src/omni.rs:906-942 (stable groups), src/benchmarking/omni.rs:277-303 (tasks) and
+    :425-437 (ascending expert order)."""
+    key = f"group_t{tokens}_p{phase}"
+    groups, order = o.group(golden[key + "_routes"])
+    exp_groups = golden[key + "_groups"]
+    for e in range(128):
+        n = int(exp_groups[e, 0])
+        assert np.array_equal(groups[e, : n + 1], exp_groups[e, : n + 1])
+    assert np.array_equal(order, golden[key + "_order"])
+    tasks = o.tasks(groups, tokens)
+    exp_tasks = golden[key + "_tasks"]
+    total = int(exp_tasks[0])
+    assert np.array_equal(tasks[: 1 + 2 * total], exp_tasks[: 1 + 2 * total])
+
+
+def test_combine_ordered_equals_unordered():
+    """src/benchmarking/omni.rs:360-442: the ordered combine is bit-identical to the
+    ascending-expert scan."""
+    from tests.golden.make_golden import expert_routes
+    tokens, width = 37, 256
+    for phase in range(3):
+        routes = expert_routes(tokens, phase == 1, phase)
+        for t in range(tokens):
+            for r in range(8):
+                routes[t, 8 + r] = o.bf16_to_f32(o.f32_to_bf16(np.float32(((r + phase) % 8 + 1) / 36)))[()]
+        i = np.arange(tokens * 8 * width)
+        values = o.f32_to_bf16(((i * 17 + phase * 7) % 251).astype(np.float32) / 128 - 1).reshape(tokens * 8, width)
+        _, order = o.group(routes)
+        a = o.combine(values, routes, order)
+        b = o.combine(values, routes, None)
+        assert np.array_equal(a, b)
+        assert np.all(np.isfinite(o.bf16_to_f32(a)))
+
+
+def test_routed_experts_match_sparse_oracle():
+    """src/omni.rs:944-1051: route -> expert(up) -> expert(up, routed) -> combine against
+    the closed-form sparse answer, INT4 tolerance 0.08."""
+    experts, topk = 128, 8
+    i = np.arange(3 * experts)
+    logits = o.f32_to_bf16(((i * 37 + i // experts * 11) % experts).astype(np.float32) / 16).reshape(3, experts)
+    j = np.arange(3 * 256)
+    x = o.f32_to_bf16((j % 17).astype(np.float32) / 16 - 0.5).reshape(3, 256)
+    rows = np.arange(experts * 256)
+    w = np.zeros((experts * 256, 256), dtype=np.float32)
+    w[rows, rows % 256] = (rows // 256 + 1).astype(np.float32) / 128
+    wt, ws = o.pack_weight(o.f32_to_bf16(w))
+    routes = o.route(logits, topk)
+    groups, _ = o.group(routes)
+    _, xc, xs, _ = o.prepare(x, 4, 256)
+    v1 = o.expert(xc, xs, wt, ws, groups, 3, 256, 256, False)
+    _, vc, vs, _ = o.prepare(v1, 4, 256)
+    v2 = o.expert(vc, vs, wt, ws, groups, 3, 256, 256, True)
+    out = o.bf16_to_f32(o.combine(v2, routes, None))
+    lf = o.bf16_to_f32(logits)
+    xf = o.bf16_to_f32(x)
+    for t in range(3):
+        ranked = sorted(range(experts), key=lambda e: -lf[t, e])
+        assert [int(q) for q in routes[t, :topk]] == ranked[:topk]
+        mx = lf[t, ranked[0]]
+        sel = [(e, np.float32(np.exp(np.float32(lf[t, e] - mx)))) for e in ranked[:topk]]
+        s = np.float32(sum(p for _, p in sel))
+        sel = sorted([(e, o.bf16_to_f32(o.f32_to_bf16(np.float32(p / s)))) for e, p in sel])
+        for c in range(256):
+            expected = np.float32(0)
+            for e, p in sel:
+                y = o.bf16_to_f32(o.f32_to_bf16(np.float32(xf[t, c] * (e + 1) / 128)))
+                y = o.bf16_to_f32(o.f32_to_bf16(np.float32(y * (e + 1) / 128)))
+                y = o.bf16_to_f32(o.f32_to_bf16(np.float32(y * p)))
+                expected = o.bf16_to_f32(o.f32_to_bf16(np.float32(expected + y)))
+            assert abs(out[t, c] - expected) <= 0.08
+
+
+def test_swiglu_within_one_bf16_step():
+    """src/ops.rs:482-525 semantics bf16(bf16(silu(g)) * u); exp bits unpinned, so compare
+    to a float64-exp restatement within one bf16 step."""
+    i = np.arange(8 * 768)
+    g = o.f32_to_bf16(((i * 17 % 1031).astype(np.float32) - 515) / 16)
+    u = o.f32_to_bf16(((i * 29 % 997).astype(np.float32) - 498) / 32)
+    out = o.bf16_to_f32(o.swiglu(g, u))
+    gf, uf = o.bf16_to_f32(g).astype(np.float64), o.bf16_to_f32(u)
+    act = o.bf16_to_f32(o.f32_to_bf16((gf / (1 + np.exp(-gf))).astype(np.float32)))
+    exp = o.bf16_to_f32(o.f32_to_bf16(act * uf))
+    assert np.all(np.abs(out - exp) <= np.abs(exp) / 128 + 1e-30)
+
+
+def test_exp_error_bound():
+    """The shared exp (Cody-Waite + degree-7 Taylor) stays within 2 ulp of float64 exp."""
+    x = np.concatenate([np.linspace(-103, 88.7, 200001, dtype=np.float32),
+                        np.array([0.0, -0.0, 1e-8, -1e-8], np.float32)])
+    got = o.exp(x).astype(np.float64)
+    ref = np.exp(x.astype(np.float64))
+    normal = ref > 1.2e-38
+    ulp = np.spacing(ref[normal].astype(np.float32)).astype(np.float64)
+    assert np.max(np.abs(got[normal] - ref[normal]) / ulp) <= 2.0
+    assert np.isinf(o.exp(np.array([89.0], np.float32))[0])
+    assert o.exp(np.array([-104.0], np.float32))[0] == 0
+    assert np.isnan(o.exp(np.array([np.nan], np.float32))[0])
