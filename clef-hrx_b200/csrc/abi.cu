@@ -1,0 +1,563 @@
+// clefq: the C ABI (include/clefq.h).  Argument checks mirror the reference's ensure!
+// conditions; every entry point is stream-ordered and allocates nothing.
+#include <mutex>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "clefq_internal.h"
+#include "cq_common.cuh"
+
+namespace cq {
+int launch_route(const void *logits, int is_f32, int64_t tokens, int experts, int topk, float *routes,
+                 cudaStream_t stream);
+int launch_group(const float *routes, int64_t tokens, int topk, int experts, int *counts, int *offsets,
+                 int *tile_list, int *perm, float *groups, float *order, float *tasks, cudaStream_t stream,
+                 int num_sms);
+int launch_tasks(const float *groups, int64_t tokens, int experts, float *tasks, cudaStream_t stream);
+int launch_groups_to_sorted(const float *groups, int64_t tokens, int topk, int experts, int *offsets, int *perm,
+                            int *tile_list, cudaStream_t stream);
+int launch_gather(const uint8_t *src, int64_t src_ld, const int *perm, int div, int64_t rows, int64_t row_bytes,
+                  uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms);
+int launch_gather_unpack_i4(const uint32_t *a, int64_t a_ld, const int *perm, int div, int64_t rows, int k,
+                            uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms);
+int launch_combine(const uint16_t *values, const float *routes, const float *order, int64_t tokens, int topk,
+                   int64_t width, uint16_t *out, cudaStream_t stream, int num_sms);
+
+// Status word set by bounded device-side waits (static: nothing is allocated for it).
+static __device__ int g_status_word;
+
+namespace {
+thread_local char g_err[512] = "";
+std::mutex g_mu;
+int g_sms[64];
+int *g_status_ptr[64];
+
+int set_err(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return code;
+}
+int cuda_err(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  return set_err(CLEFQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d < 0 || d >= 64 ? 0 : d;
+}
+
+// Bump allocator over a caller workspace (256-byte aligned sections).
+struct Arena {
+  uint8_t *base;
+  int64_t cap, used = 0;
+  bool ok = true;
+  template <class T>
+  T *take(int64_t count) {
+    int64_t off = (used + 255) & ~int64_t(255);
+    int64_t bytes = count * (int64_t)sizeof(T);
+    if (off + bytes > cap) {
+      ok = false;
+      return nullptr;
+    }
+    used = off + bytes;
+    return base ? reinterpret_cast<T *>(base + off) : nullptr;
+  }
+};
+int64_t aligned_total(const Arena &a) { return (a.used + 255) & ~int64_t(255); }
+
+bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+}  // namespace
+
+int device_sms() {
+  const int d = current_device();
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_sms[d]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d);
+    g_sms[d] = v > 0 ? v : 148;
+  }
+  return g_sms[d];
+}
+
+int *device_status_word() {
+  const int d = current_device();
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_status_ptr[d]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    g_status_ptr[d] = static_cast<int *>(p);
+  }
+  return g_status_ptr[d];
+}
+
+// ---- validation shared by the packing entry points (src/quantized.rs:621-640) --------
+static int check_prepare(int kind, int bits, int64_t rows, int64_t width, int64_t stride) {
+  if (!(bits == 4 || bits == 8)) return set_err(CLEFQ_ERR_SHAPE, "unsupported rotated integer operand: bits=%d", bits);
+  if (kind < 0 || kind > 4) return set_err(CLEFQ_ERR_SHAPE, "unknown packing kind %d", kind);
+  if (width < 256 || width > 32768 || width % 256)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported rotated integer operand: width=%lld", (long long)width);
+  if (rows < 1 || rows > 1048576)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported rotated integer operand: rows=%lld", (long long)rows);
+  if (stride < width || stride > 65536 || stride % (512 / bits))
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported rotated integer operand: stride=%lld", (long long)stride);
+  return 0;
+}
+
+static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_t x_ld, const void *aux,
+                       int64_t aux_ld, int64_t rows, int64_t width, int64_t stride, void *out, void *operand,
+                       int64_t operand_ld, void *norm_out, int64_t norm_ld) {
+  int rc = check_prepare(kind, bits, rows, width, stride);
+  if (rc) return rc;
+  if (!x || !out || (kind != CLEFQ_PREP_PLAIN && !aux) || (kind == CLEFQ_PREP_NORM_STORE && !norm_out))
+    return set_err(CLEFQ_ERR_SHAPE, "packing input count");
+  if (x_ld < width || !al16(x) || (x_ld * 2) % 16) return set_err(CLEFQ_ERR_ALIGN, "x must be 16-byte aligned rows");
+  if (kind == CLEFQ_PREP_SWIGLU && (aux_ld < width || !al16(aux) || (aux_ld * 2) % 16))
+    return set_err(CLEFQ_ERR_SHAPE, "packing input shape/dtype mismatch");
+  if (kind == CLEFQ_PREP_ATTN_GATE && (aux_ld < 2 * width || !al16(aux) || (aux_ld * 2) % 16))
+    return set_err(CLEFQ_ERR_SHAPE, "attention packing input count");
+  if ((kind == CLEFQ_PREP_NORM || kind == CLEFQ_PREP_NORM_STORE) && !al16(aux))
+    return set_err(CLEFQ_ERR_ALIGN, "norm weight must be 16-byte aligned");
+  if (kind == CLEFQ_PREP_NORM_STORE && (norm_ld < width || !al16(norm_out) || (norm_ld * 2) % 16))
+    return set_err(CLEFQ_ERR_ALIGN, "norm output must be 16-byte aligned rows");
+  if (operand) {
+    if (bits != 4) return set_err(CLEFQ_ERR_SHAPE, "the s8 operand output is for 4-bit codes");
+    if (operand_ld < width || !al16(operand) || operand_ld % 16)
+      return set_err(CLEFQ_ERR_ALIGN, "operand must be 16-byte aligned rows of >= width bytes");
+  }
+  if ((uintptr_t)out % 8) return set_err(CLEFQ_ERR_ALIGN, "packed output must be 8-byte aligned");
+  PrepareArgs a{};
+  a.x = static_cast<const uint16_t *>(x);
+  a.x_ld = x_ld;
+  a.aux = static_cast<const uint16_t *>(aux);
+  a.aux_ld = aux_ld;
+  a.rows = rows;
+  a.width = (int)width;
+  a.stride = (int)stride;
+  a.bits = bits;
+  a.mode = kind;
+  a.out = static_cast<uint32_t *>(out);
+  a.op8 = static_cast<uint8_t *>(operand);
+  a.op_ld = operand_ld;
+  a.norm_out = static_cast<uint16_t *>(norm_out);
+  a.norm_ld = norm_ld;
+  rc = launch_prepare(a, s);
+  return rc ? cuda_err("prepare launch") : 0;
+}
+
+static int run_gemm(cudaStream_t s, int bits, const uint8_t *op, int64_t op_ld, int64_t op_rows, const float *a_scales,
+                    int64_t m, const void *w0, const float *ws0, const void *w1, const float *ws1, int n_split, int64_t n,
+                    int64_t k, const void *residual, int64_t residual_ld, int out_dtype, void *out, int64_t out_ld) {
+  int *status = device_status_word();
+  if (!status) return cuda_err("status word");
+  GemmParams p{};
+  p.a_op = op;
+  p.a_rows = op_rows;
+  p.a_ld = op_ld;
+  p.a_scales = a_scales;
+  p.w[0] = static_cast<const uint32_t *>(w0);
+  p.w[1] = static_cast<const uint32_t *>(w1);
+  p.w_scales[0] = ws0;
+  p.w_scales[1] = ws1;
+  p.n_split = n_split;
+  p.m = m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.bits = bits;
+  p.out = out_dtype == CLEFQ_BF16 ? static_cast<uint16_t *>(out) : nullptr;
+  p.out_f32 = out_dtype == CLEFQ_F32 ? static_cast<float *>(out) : nullptr;
+  p.ldo = out_ld;
+  p.residual = static_cast<const uint16_t *>(residual);
+  p.ldr = residual_ld;
+  p.err = status;
+  int rc = launch_gemm(p, s);
+  if (rc == CLEFQ_ERR_CUDA) return cuda_err("gemm launch");
+  if (rc) return set_err(rc, "unsupported integer GEMM shape or alignment (n %% 128, k %% 256, 16-byte operand rows)");
+  return 0;
+}
+
+static int check_gemm(int bits, int64_t m, int64_t n, int64_t k, int64_t a_cols, const void *residual,
+                      int64_t residual_ld, int out_dtype, int64_t out_ld) {
+  if (!(bits == 4 || bits == 8)) return set_err(CLEFQ_ERR_SHAPE, "integer projections need 4 or 8 bits");
+  if (m < 0 || m > 16777216) return set_err(CLEFQ_ERR_SHAPE, "row count out of range");
+  if (n < 128 || n > 65536 || n % 128) return set_err(CLEFQ_ERR_SHAPE, "n must be a multiple of 128 in [128, 65536]");
+  if (k < 256 || k > 65536 || k % 256) return set_err(CLEFQ_ERR_SHAPE, "k must be a multiple of 256 in [256, 65536]");
+  if (a_cols < k) return set_err(CLEFQ_ERR_SHAPE, "quantized projection shape/dtype mismatch");
+  if (out_dtype != CLEFQ_BF16 && out_dtype != CLEFQ_F32) return set_err(CLEFQ_ERR_SHAPE, "unknown output dtype");
+  if (out_ld < n) return set_err(CLEFQ_ERR_SHAPE, "output pitch below n");
+  if (residual && (out_dtype != CLEFQ_BF16 || residual_ld < n))
+    return set_err(CLEFQ_ERR_SHAPE, "projection residual shape/dtype mismatch");
+  return 0;
+}
+
+}  // namespace cq
+
+using namespace cq;
+
+extern "C" {
+
+const char *clefq_last_error(void) { return g_err; }
+int clefq_version(void) { return 100; }
+
+int clefq_status(void *stream) {
+  int *w = device_status_word();
+  if (!w) return cuda_err("status word");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return cuda_err("stream");
+  int v = 0;
+  if (cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return cuda_err("status read");
+  if (v) {
+    int zero = 0;
+    cudaMemcpy(w, &zero, sizeof zero, cudaMemcpyHostToDevice);
+    return set_err(CLEFQ_ERR_TIMEOUT, "a device-side wait gave up (site %d)", v);
+  }
+  return 0;
+}
+
+int clefq_prepare(void *stream, int kind, int bits, const void *x, int64_t x_ld, const void *aux, int64_t aux_ld,
+                  int64_t rows, int64_t width, int64_t stride, void *out, void *operand, int64_t operand_ld,
+                  void *norm_out, int64_t norm_ld) {
+  return run_prepare(static_cast<cudaStream_t>(stream), kind, bits, x, x_ld, aux, aux_ld, rows, width, stride, out,
+                     operand, operand_ld, norm_out, norm_ld);
+}
+
+int clefq_retile(void *stream, const void *codes, int64_t rows, int64_t cols, int bits, int64_t in_words, void *out) {
+  if (!(bits == 4 || bits == 8)) return set_err(CLEFQ_ERR_SHAPE, "unsupported packed weight shape for tiling");
+  const int64_t words = cols / (32 / bits);
+  if (rows <= 0 || rows % 128 || cols % (32 / bits) || words % 32 || in_words < words)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported packed weight shape for tiling");
+  if (!al16(codes) || !al16(out)) return set_err(CLEFQ_ERR_ALIGN, "codes/out must be 16-byte aligned");
+  int rc = launch_retile(static_cast<const uint32_t *>(codes), rows, in_words, words, static_cast<uint32_t *>(out),
+                         static_cast<cudaStream_t>(stream), device_sms());
+  return rc ? cuda_err("retile launch") : 0;
+}
+
+int64_t clefq_gemm_workspace_size(int64_t m, int64_t k, int bits) { return bits == 4 ? ((m * k + 255) & ~255LL) : 0; }
+
+int clefq_gemm(void *stream, int bits, const void *a_codes, int64_t a_ld_words, const float *a_scales, int64_t m,
+               const void *w_tiled, const float *w_scales, int64_t n, int64_t k, const void *residual,
+               int64_t residual_ld, int out_dtype, void *out, int64_t out_ld, void *workspace,
+               int64_t workspace_bytes) {
+  int rc = check_gemm(bits, m, n, k, a_ld_words * (32 / bits), residual, residual_ld, out_dtype, out_ld);
+  if (rc) return rc;
+  if (m == 0) return 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bits == 8) {
+    if ((a_ld_words * 4) % 16 || !al16(a_codes))
+      return set_err(CLEFQ_ERR_ALIGN, "8-bit codes are read in place: 16-byte aligned rows needed");
+    return run_gemm(s, 8, static_cast<const uint8_t *>(a_codes), a_ld_words * 4, m, a_scales, m, w_tiled, w_scales,
+                    nullptr, nullptr, (int)(n / 128), n, k, residual, residual_ld, out_dtype, out, out_ld);
+  }
+  if (!workspace || workspace_bytes < clefq_gemm_workspace_size(m, k, 4))
+    return set_err(CLEFQ_ERR_WORKSPACE, "gemm workspace must hold m*k bytes");
+  if (!al16(workspace)) return set_err(CLEFQ_ERR_ALIGN, "workspace must be 16-byte aligned");
+  uint8_t *op = static_cast<uint8_t *>(workspace);
+  rc = launch_unpack_i4(static_cast<const uint32_t *>(a_codes), a_ld_words, m, (int)k, op, k, s, device_sms());
+  if (rc) return cuda_err("unpack launch");
+  return run_gemm(s, 4, op, k, m, a_scales, m, w_tiled, w_scales, nullptr, nullptr, (int)(n / 128), n, k, residual,
+                  residual_ld, out_dtype, out, out_ld);
+}
+
+int clefq_gemm_s8(void *stream, int bits, const void *operand, int64_t operand_ld, const float *a_scales, int64_t m,
+                  const void *w_tiled, const float *w_scales, int64_t n, int64_t k, const void *residual,
+                  int64_t residual_ld, int out_dtype, void *out, int64_t out_ld) {
+  int rc = check_gemm(bits, m, n, k, operand_ld, residual, residual_ld, out_dtype, out_ld);
+  if (rc) return rc;
+  if (m == 0) return 0;
+  return run_gemm(static_cast<cudaStream_t>(stream), bits, static_cast<const uint8_t *>(operand), operand_ld, m,
+                  a_scales, m, w_tiled, w_scales, nullptr, nullptr, (int)(n / 128), n, k, residual, residual_ld,
+                  out_dtype, out, out_ld);
+}
+
+int clefq_swiglu(void *stream, const void *gate, const void *up, int64_t n, void *out) {
+  if (n < 0) return set_err(CLEFQ_ERR_SHAPE, "SwiGLU shape/dtype mismatch");
+  if (n == 0) return 0;
+  int rc = launch_swiglu(static_cast<const uint16_t *>(gate), static_cast<const uint16_t *>(up),
+                         static_cast<uint16_t *>(out), n, static_cast<cudaStream_t>(stream), device_sms());
+  return rc ? cuda_err("swiglu launch") : 0;
+}
+
+int clefq_route(void *stream, const void *logits, int logits_dtype, int64_t tokens, int experts, int topk,
+                float *routes) {
+  if (!(topk > 0 && topk <= experts && experts <= 128 && topk <= 32))
+    return set_err(CLEFQ_ERR_SHAPE, "invalid expert router shape");
+  if (logits_dtype != CLEFQ_BF16 && logits_dtype != CLEFQ_F32) return set_err(CLEFQ_ERR_SHAPE, "logits dtype");
+  if (tokens < 0) return set_err(CLEFQ_ERR_SHAPE, "invalid expert router shape");
+  int rc = launch_route(logits, logits_dtype == CLEFQ_F32, tokens, experts, topk, routes,
+                        static_cast<cudaStream_t>(stream));
+  return rc ? cuda_err("route launch") : 0;
+}
+
+static Arena group_tables(Arena a, int64_t tokens, int topk, int experts, int **counts, int **offsets, int **tiles,
+                          int **perm) {
+  const int64_t routes = tokens * topk;
+  *counts = a.take<int>(experts);
+  *offsets = a.take<int>(experts + 1);
+  *tiles = a.take<int>(1 + 2 * ((routes + 127) / 128 + experts));
+  *perm = a.take<int>(routes > 0 ? routes : 1);
+  return a;
+}
+
+int64_t clefq_group_workspace_size(int64_t tokens, int topk, int experts) {
+  int *c, *o, *t, *p;
+  Arena a{nullptr, INT64_MAX};
+  a = group_tables(a, tokens, topk, experts, &c, &o, &t, &p);
+  return aligned_total(a);
+}
+
+int clefq_group_routes(void *stream, const float *routes, int64_t tokens, int topk, int experts, float *groups,
+                       float *order, void *workspace, int64_t workspace_bytes) {
+  if (tokens < 1 || tokens > 1048576 || topk < 1 || topk > 32 || experts < 1 || experts > 1024)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported Omni route grouping shape");
+  int *counts, *offsets, *tiles, *perm;
+  Arena a = group_tables(Arena{static_cast<uint8_t *>(workspace), workspace_bytes}, tokens, topk, experts, &counts,
+                         &offsets, &tiles, &perm);
+  if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "group workspace too small");
+  int rc = launch_group(routes, tokens, topk, experts, counts, offsets, tiles, perm, groups, order, nullptr,
+                        static_cast<cudaStream_t>(stream), device_sms());
+  return rc ? cuda_err("group launch") : 0;
+}
+
+int clefq_expert_tasks(void *stream, const float *groups, int64_t tokens, int experts, float *tasks) {
+  if (tokens < 1 || experts < 1 || experts > 1024) return set_err(CLEFQ_ERR_SHAPE, "unsupported compact Omni routes");
+  int rc = launch_tasks(groups, tokens, experts, tasks, static_cast<cudaStream_t>(stream));
+  return rc ? cuda_err("tasks launch") : 0;
+}
+
+static Arena expert_tables(Arena a, int64_t tokens, int topk, int experts, int64_t k, int **offsets, int **tiles,
+                           int **perm, uint8_t **op) {
+  const int64_t routes = tokens * topk;
+  *offsets = a.take<int>(experts + 1);
+  *tiles = a.take<int>(1 + 2 * ((routes + 127) / 128 + experts));
+  *perm = a.take<int>(routes > 0 ? routes : 1);
+  *op = a.take<uint8_t>(routes * k);
+  return a;
+}
+
+int64_t clefq_expert_workspace_size(int64_t tokens, int topk, int experts, int64_t k) {
+  int *o, *t, *p;
+  uint8_t *op;
+  Arena a{nullptr, INT64_MAX};
+  a = expert_tables(a, tokens, topk, experts, k, &o, &t, &p, &op);
+  return aligned_total(a);
+}
+
+int clefq_expert(void *stream, const void *a_codes, int64_t a_ld_words, const float *a_scales, const void *w_tiled,
+                 const float *w_scales, const float *groups, int64_t tokens, int topk, int experts, int64_t k,
+                 int64_t n, int input_routed, void *out, void *workspace, int64_t workspace_bytes) {
+  if (tokens < 1 || tokens > 1048576 || topk < 1 || topk > 32 || experts < 1 || experts > 1024)
+    return set_err(CLEFQ_ERR_SHAPE, "invalid grouped expert routes");
+  if (n < 128 || n % 128 || k < 256 || k % 256 || a_ld_words * 8 < k)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported Omni expert tile shape");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int *offsets, *tiles, *perm;
+  uint8_t *op;
+  Arena a = expert_tables(Arena{static_cast<uint8_t *>(workspace), workspace_bytes}, tokens, topk, experts, k,
+                          &offsets, &tiles, &perm, &op);
+  if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "expert workspace too small");
+  const int64_t routes = tokens * topk;
+  int rc = launch_groups_to_sorted(groups, tokens, topk, experts, offsets, perm, tiles, s);
+  if (!rc)
+    rc = launch_gather_unpack_i4(static_cast<const uint32_t *>(a_codes), a_ld_words, perm, input_routed ? 1 : topk,
+                                 routes, (int)k, op, k, s, device_sms());
+  if (rc) return cuda_err("expert table launch");
+  int *status = device_status_word();
+  if (!status) return cuda_err("status word");
+  GemmParams p{};
+  p.a_op = op;
+  p.a_rows = routes;
+  p.a_ld = k;
+  p.a_scales = a_scales;
+  p.w[0] = static_cast<const uint32_t *>(w_tiled);
+  p.w_scales[0] = w_scales;
+  p.n_split = (int)(n / 128);
+  p.n = (int)n;
+  p.k = (int)k;
+  p.bits = 4;
+  p.out = static_cast<uint16_t *>(out);
+  p.ldo = n;
+  p.grouped = 1;
+  p.tile_list = tiles;
+  p.expert_offsets = offsets;
+  p.perm = perm;
+  p.max_tiles = (int)((routes + 127) / 128 + experts);
+  p.topk = topk;
+  p.scale_mode = input_routed ? 2 : 1;
+  p.scatter = 1;
+  p.err = status;
+  rc = launch_gemm(p, s);
+  if (rc == CLEFQ_ERR_CUDA) return cuda_err("expert gemm launch");
+  return rc ? set_err(rc, "unsupported Omni expert tile shape") : 0;
+}
+
+int clefq_combine(void *stream, const void *values, const float *routes, const float *order, int64_t tokens, int topk,
+                  int64_t width, void *out) {
+  if (width % 8 || width <= 0 || topk < 1 || topk > 32 || tokens < 0)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported ordered Omni accumulation");
+  int rc = launch_combine(static_cast<const uint16_t *>(values), routes, order, tokens, topk, width,
+                          static_cast<uint16_t *>(out), static_cast<cudaStream_t>(stream), device_sms());
+  if (rc == CLEFQ_ERR_ALIGN) return set_err(rc, "values/out must be 16-byte aligned");
+  return rc ? cuda_err("combine launch") : 0;
+}
+
+// ---- fused dense MLP -------------------------------------------------------------------
+static int64_t stride_for(int64_t k) { return k + (k % 1024 == 0 ? 128 : 0); }
+
+static Arena mlp_tables(Arena a, int64_t m, int64_t hidden, int64_t inter, uint32_t **xq, uint8_t **x8, uint16_t **gu,
+                        uint32_t **hq, uint8_t **h8) {
+  *xq = a.take<uint32_t>(m * (stride_for(hidden) / 8 + 1));
+  *x8 = a.take<uint8_t>(m * hidden);
+  *gu = a.take<uint16_t>(m * 2 * inter);
+  *hq = a.take<uint32_t>(m * (stride_for(inter) / 8 + 1));
+  *h8 = a.take<uint8_t>(m * inter);
+  return a;
+}
+
+int64_t clefq_mlp_workspace_size(int64_t m, int64_t hidden, int64_t inter) {
+  uint32_t *xq, *hq;
+  uint8_t *x8, *h8;
+  uint16_t *gu;
+  Arena a{nullptr, INT64_MAX};
+  a = mlp_tables(a, m, hidden, inter, &xq, &x8, &gu, &hq, &h8);
+  return aligned_total(a);
+}
+
+int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t inter, const void *gate_tiled,
+              const float *gate_scales, const void *up_tiled, const float *up_scales, const void *down_tiled,
+              const float *down_scales, const void *residual, void *out, void *workspace, int64_t workspace_bytes) {
+  if (m < 1 || hidden % 256 || inter % 256 || hidden < 256 || inter < 256 || hidden > 32768 || inter > 32768)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported MLP shape");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t *xq, *hq;
+  uint8_t *x8, *h8;
+  uint16_t *gu;
+  Arena a = mlp_tables(Arena{static_cast<uint8_t *>(workspace), workspace_bytes}, m, hidden, inter, &xq, &x8, &gu, &hq,
+                       &h8);
+  if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "mlp workspace too small");
+  const int64_t sh = stride_for(hidden), si = stride_for(inter);
+  int rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, m, hidden, sh, xq, x8, hidden, nullptr, 0);
+  if (rc) return rc;
+  // gate and up in one launch: output columns [0, inter) gate, [inter, 2*inter) up
+  rc = run_gemm(s, 4, x8, hidden, m, reinterpret_cast<const float *>(xq + m * (sh / 8)), m, gate_tiled, gate_scales,
+                up_tiled, up_scales, (int)(inter / 128), 2 * inter, hidden, nullptr, 0, CLEFQ_BF16, gu, 2 * inter);
+  if (rc) return rc;
+  rc = run_prepare(s, CLEFQ_PREP_SWIGLU, 4, gu, 2 * inter, gu + inter, 2 * inter, m, inter, si, hq, h8, inter, nullptr,
+                   0);
+  if (rc) return rc;
+  return run_gemm(s, 4, h8, inter, m, reinterpret_cast<const float *>(hq + m * (si / 8)), m, down_tiled, down_scales,
+                  nullptr, nullptr, (int)(hidden / 128), hidden, inter, residual, hidden, CLEFQ_BF16, out, hidden);
+}
+
+// ---- fused Omni MoE block --------------------------------------------------------------
+struct MoeTables {
+  float *routes, *order;
+  int *counts, *offsets, *tiles, *perm;
+  uint32_t *xq, *hq;
+  uint8_t *x8, *xs, *h8;
+  uint16_t *gu, *values;
+};
+static Arena moe_tables(Arena a, int64_t tokens, int64_t hidden, int64_t inter, int experts, int topk, MoeTables &t) {
+  const int64_t routes = tokens * topk;
+  t.routes = a.take<float>(tokens * 2 * topk);
+  t.order = a.take<float>(tokens * topk);
+  t.counts = a.take<int>(experts);
+  t.offsets = a.take<int>(experts + 1);
+  t.tiles = a.take<int>(1 + 2 * ((routes + 127) / 128 + experts));
+  t.perm = a.take<int>(routes);
+  t.xq = a.take<uint32_t>(tokens * (stride_for(hidden) / 8 + 1));
+  t.x8 = a.take<uint8_t>(tokens * hidden);
+  t.xs = a.take<uint8_t>(routes * hidden);
+  t.gu = a.take<uint16_t>(routes * 2 * inter);
+  t.hq = a.take<uint32_t>(routes * (inter / 8 + 1));
+  t.h8 = a.take<uint8_t>(routes * inter);
+  t.values = a.take<uint16_t>(routes * hidden);
+  return a;
+}
+
+int64_t clefq_moe_workspace_size(int64_t tokens, int64_t hidden, int64_t inter, int experts, int topk) {
+  MoeTables t;
+  Arena a{nullptr, INT64_MAX};
+  a = moe_tables(a, tokens, hidden, inter, experts, topk, t);
+  return aligned_total(a);
+}
+
+int clefq_moe(void *stream, const void *x, const void *logits, int logits_dtype, int64_t tokens, int64_t hidden,
+              int64_t inter, int experts, int topk, const void *gate_tiled, const float *gate_scales,
+              const void *up_tiled, const float *up_scales, const void *down_tiled, const float *down_scales,
+              void *out, float *routes_out, void *workspace, int64_t workspace_bytes) {
+  if (tokens < 1 || tokens > 1048576 || hidden % 256 || inter % 256 || hidden < 256 || inter < 256 ||
+      hidden > 32768 || inter > 32768 || !(topk > 0 && topk <= experts && experts <= 128 && topk <= 32))
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported Omni MoE shape");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  MoeTables t;
+  Arena a = moe_tables(Arena{static_cast<uint8_t *>(workspace), workspace_bytes}, tokens, hidden, inter, experts, topk,
+                       t);
+  if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "moe workspace too small");
+  float *routes = routes_out ? routes_out : t.routes;
+  const int64_t nroutes = tokens * topk;
+  const int sms = device_sms();
+  int rc = launch_route(logits, logits_dtype == CLEFQ_F32, tokens, experts, topk, routes, s);
+  if (!rc)
+    rc = launch_group(routes, tokens, topk, experts, t.counts, t.offsets, t.tiles, t.perm, nullptr, t.order, nullptr,
+                      s, sms);
+  if (rc) return cuda_err("routing launch");
+  const int64_t sh = stride_for(hidden);
+  rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, tokens, hidden, sh, t.xq, t.x8, hidden, nullptr, 0);
+  if (rc) return rc;
+  rc = launch_gather(t.x8, hidden, t.perm, topk, nroutes, hidden, t.xs, hidden, s, sms);
+  if (rc) return cuda_err("gather launch");
+  int *status = device_status_word();
+  if (!status) return cuda_err("status word");
+  GemmParams p{};
+  p.a_op = t.xs;
+  p.a_rows = nroutes;
+  p.a_ld = hidden;
+  p.a_scales = reinterpret_cast<const float *>(t.xq + tokens * (sh / 8));
+  p.w[0] = static_cast<const uint32_t *>(gate_tiled);
+  p.w[1] = static_cast<const uint32_t *>(up_tiled);
+  p.w_scales[0] = gate_scales;
+  p.w_scales[1] = up_scales;
+  p.n_split = (int)(inter / 128);
+  p.n = (int)(2 * inter);
+  p.k = (int)hidden;
+  p.bits = 4;
+  p.out = t.gu;
+  p.ldo = 2 * inter;
+  p.grouped = 1;
+  p.tile_list = t.tiles;
+  p.expert_offsets = t.offsets;
+  p.perm = t.perm;
+  p.max_tiles = (int)((nroutes + 127) / 128 + experts);
+  p.topk = topk;
+  p.scale_mode = 1;  // activation scale of the token
+  p.scatter = 0;     // rows stay in expert-sorted order
+  p.err = status;
+  rc = launch_gemm(p, s);
+  if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert gate/up launch") : set_err(rc, "expert gate/up shape");
+  // SwiGLU fused into the packing of the hidden rows (still expert-sorted).
+  rc = run_prepare(s, CLEFQ_PREP_SWIGLU, 4, t.gu, 2 * inter, t.gu + inter, 2 * inter, nroutes, inter, inter, t.hq, t.h8,
+                   inter, nullptr, 0);
+  if (rc) return rc;
+  p.a_op = t.h8;
+  p.a_ld = inter;
+  p.a_scales = reinterpret_cast<const float *>(t.hq + nroutes * (inter / 8));
+  p.w[0] = static_cast<const uint32_t *>(down_tiled);
+  p.w[1] = nullptr;
+  p.w_scales[0] = down_scales;
+  p.w_scales[1] = nullptr;
+  p.n_split = (int)(hidden / 128);
+  p.n = (int)hidden;
+  p.k = (int)inter;
+  p.out = t.values;
+  p.ldo = hidden;
+  p.scale_mode = 0;  // hidden rows were packed in sorted order
+  p.scatter = 1;     // values land at their route id
+  rc = launch_gemm(p, s);
+  if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert down launch") : set_err(rc, "expert down shape");
+  rc = launch_combine(t.values, routes, t.order, tokens, topk, hidden, static_cast<uint16_t *>(out), s, sms);
+  return rc ? cuda_err("combine launch") : 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,69 @@
+// clefq: internal launch interfaces shared by the .cu files (not part of the C ABI).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/clefq.h"
+
+namespace cq {
+
+struct PrepareArgs {
+  const uint16_t *x;
+  int64_t x_ld;
+  const uint16_t *aux;  // SwiGLU up [rows][aux_ld], attention q_gate [rows][aux_ld], norm weight [width]
+  int64_t aux_ld;
+  int64_t rows;
+  int width;
+  int stride;
+  int bits;
+  int mode;
+  uint32_t *out;        // codes then scales
+  uint8_t *op8;         // optional s8 operand [rows][op_ld] (int4 only)
+  int64_t op_ld;
+  uint16_t *norm_out;   // MODE_NORM_STORE: bf16 [rows][norm_ld]
+  int64_t norm_ld;
+  int team_warps;       // warps per row (set by launch_prepare)
+  int rows_per_block;
+};
+int launch_prepare(const PrepareArgs &a, cudaStream_t stream);
+int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);
+int launch_retile(const uint32_t *codes, int64_t rows, int64_t in_words, int64_t words, uint32_t *out,
+                  cudaStream_t stream, int num_sms);
+int launch_unpack_i4(const uint32_t *a, int64_t a_ld, int64_t rows, int k, uint8_t *op, int64_t op_ld,
+                     cudaStream_t stream, int num_sms);
+
+// Dense / grouped tcgen05 GEMM over an s8 token operand and tiled int4/int8 weights.
+struct GemmParams {
+  const uint8_t *a_op;      // s8 token operand [rows][a_ld bytes]
+  int64_t a_rows;           // rows of the operand tensor (TMA bound)
+  int64_t a_ld;             // bytes
+  const float *a_scales;
+  const uint32_t *w[2];     // tiled codes: one matrix, or two stacked along the output
+  const float *w_scales[2]; //   columns (e.g. gate then up), each n_split*128 rows per expert
+  int n_split;              // 128-row weight tiles per matrix per expert
+  int64_t m;                // dense: token rows
+  int n;                    // output columns (both matrices; per expert when grouped)
+  int k;
+  int bits;
+  uint16_t *out;            // bf16 [.][ldo]
+  float *out_f32;           // optional f32 output (dense)
+  int64_t ldo;
+  const uint16_t *residual; // optional bf16 residual [m][ldr] (dense)
+  int64_t ldr;
+  // grouped (MoE) mode
+  int grouped;
+  const int *tile_list;     // [1 + 2*max_tiles]: count, then (expert, sorted_row0)
+  const int *expert_offsets;// [experts + 1] sorted-row offsets
+  const int *perm;          // sorted position -> route id
+  int max_tiles;
+  int topk;
+  int scale_mode;           // a_scales index: 0 -> p, 1 -> perm[p] / topk, 2 -> perm[p]
+  int scatter;              // output row: 1 -> perm[p], 0 -> p
+  int *err;                 // device status word
+};
+int launch_gemm(const GemmParams &p, cudaStream_t stream);
+
+int device_sms();
+int *device_status_word();  // per-device zero-initialised status word used by bounded waits
+
+}  // namespace cq

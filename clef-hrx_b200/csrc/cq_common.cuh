@@ -1,0 +1,227 @@
+// clefq: shared device helpers for the sm_100a kernels.
+//
+// Numerics: IEEE binary32 with round-to-nearest-even; every multiply and add whose
+// rounding is part of the reference contract is written with __fmul_rn / __fadd_rn /
+// __fsub_rn / __fmaf_rn so the compiler cannot contract or reassociate it.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#define CQ_DEV __device__ __forceinline__
+
+namespace cq {
+
+// ---------------------------------------------------------------------------------------
+// BF16 <-> F32, round to nearest even (the reference's `half` crate and Loom fptrunc);
+// NaN keeps its sign and top payload bits with the quiet bit set.
+// ---------------------------------------------------------------------------------------
+CQ_DEV float bf16_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+CQ_DEV uint16_t f32_to_bf16(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x0040u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+CQ_DEV float bf16r(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+// exp(x): Cody & Waite (1980) two-constant argument reduction x = n ln2 + r, |r| <= ln2/2,
+// degree-7 Taylor polynomial of e^r in Horner form with fused multiply-adds, and exact
+// scaling by 2^n split into two powers of two.  Error below 2 ulp over the normal range;
+// the CPU oracle evaluates the identical steps, so the two agree bit for bit.
+CQ_DEV float pow2i(int n) { return __uint_as_float((uint32_t)(n + 127) << 23); }
+CQ_DEV float exp_cw(float x) {
+  if (x != x) return x;
+  if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+  if (x < -103.972084045410156f) return 0.0f;
+  const float log2e = 1.44269502162933349609375f;
+  const float ln2_hi = 0.693145751953125f;
+  const float ln2_lo = 1.428606765330187045e-06f;
+  float n = rintf(__fmul_rn(x, log2e));
+  float r = __fmaf_rn(-n, ln2_hi, x);
+  r = __fmaf_rn(-n, ln2_lo, r);
+  float p = 1.0f / 5040.0f;
+  p = __fmaf_rn(p, r, 1.0f / 720.0f);
+  p = __fmaf_rn(p, r, 1.0f / 120.0f);
+  p = __fmaf_rn(p, r, 1.0f / 24.0f);
+  p = __fmaf_rn(p, r, 1.0f / 6.0f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  int ni = (int)n;
+  int n1 = ni / 2;
+  int n2 = ni - n1;
+  return __fmul_rn(__fmul_rn(p, pow2i(n1)), pow2i(n2));
+}
+
+// IEEE maxNum / minNum (return the non-NaN operand).
+CQ_DEV float maxnum(float a, float b) { return fmaxf(a, b); }
+CQ_DEV float minnum(float a, float b) { return fminf(a, b); }
+
+// The s8 GEMM operand of a packed int4 word: 16 * code, K-permuted within each 32-code
+// group (low nibbles of the 4 words first, then high nibbles).  Both GEMM operands use
+// the same permutation, so dot products are unchanged; the x16 on each side makes every
+// accumulator exactly 256 * the reference's int32 dot.
+CQ_DEV uint32_t nib_lo16(uint32_t w) { return (w << 4) & 0xF0F0F0F0u; }
+CQ_DEV uint32_t nib_hi16(uint32_t w) { return w & 0xF0F0F0F0u; }
+
+// ---------------------------------------------------------------------------------------
+// Shared-memory addresses, mbarriers, TMA, tcgen05 (inline PTX for sm_100a)
+// ---------------------------------------------------------------------------------------
+CQ_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+CQ_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+CQ_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+CQ_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+CQ_DEV void mbar_arrive(uint64_t *bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+CQ_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+CQ_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+CQ_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: polls for at most ~2 s of wall time, then records `code` in *err and
+// returns false.  The caller then skips the rest of its role; the kernel still frees its
+// TMEM and exits, so a lost arrival shows up as an error status, never as a hang.
+// A wait also gives up early once another role of the same CTA has reported an error.
+CQ_DEV bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*(volatile int *)err) return false;
+    if (globaltimer_ns() - t0 > 2000000000ull) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+struct alignas(64) TmaDesc {
+  uint8_t bytes[128];
+};
+
+CQ_DEV void tma_prefetch_desc(const void *desc) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(desc) : "memory");
+}
+
+// 2D tiled TMA load (no multicast) into CTA shared memory, completing on `bar`.
+CQ_DEV void tma_load_2d(void *dst, const void *desc, uint64_t *bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(desc), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// --- tcgen05 ---------------------------------------------------------------------------
+CQ_DEV void tmem_alloc(uint32_t *slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+               "r"(ncols)
+               : "memory");
+}
+CQ_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+CQ_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+CQ_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+CQ_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] x B[smem desc], kind::i8 (s8 x s8 -> s32), one CTA.
+CQ_DEV void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on `bar` once every previously issued tcgen05.mma of this thread has completed.
+CQ_DEV void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Instruction descriptor: kind::i8, D s32, A s8, B s8, both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle, 8-row core groups 1024 B
+// apart (SBO), version 1 (sm_100).  `addr` is the byte address in shared memory.
+CQ_DEV uint64_t smem_desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;              // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;    // SBO
+  d |= (uint64_t)1u << 46;              // version
+  d |= (uint64_t)2u << 61;              // SWIZZLE_128B
+  return d;
+}
+
+// 32 lanes x 32-bit, 64 consecutive columns per thread.
+CQ_DEV void tmem_st_x64(uint32_t taddr, const uint32_t (&v)[64]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {"
+      "%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,"
+      "%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,"
+      "%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]), "r"(v[32]), "r"(v[33]), "r"(v[34]), "r"(v[35]), "r"(v[36]),
+      "r"(v[37]), "r"(v[38]), "r"(v[39]), "r"(v[40]), "r"(v[41]), "r"(v[42]), "r"(v[43]), "r"(v[44]), "r"(v[45]),
+      "r"(v[46]), "r"(v[47]), "r"(v[48]), "r"(v[49]), "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]),
+      "r"(v[55]), "r"(v[56]), "r"(v[57]), "r"(v[58]), "r"(v[59]), "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63])
+      : "memory");
+}
+CQ_DEV void tmem_st_x32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {"
+      "%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+CQ_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+CQ_DEV void tmem_ld_x32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+CQ_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+CQ_DEV uint4 ldg_nc_v4(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+
+}  // namespace cq

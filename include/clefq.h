@@ -1,0 +1,204 @@
+/*
+ * clefq -- C ABI of the B200 (sm_100a) implementation of clef-hrx's INT4 quantized
+ * matmul path: activation/weight packing, the dense INT4 GEMM and SwiGLU MLP, and the
+ * Omni MoE expert pipeline (route, group, grouped expert GEMMs, combine).
+ *
+ * Conventions (all entry points):
+ *   - Every call is asynchronous and stream-ordered on `stream` (a cudaStream_t; NULL is
+ *     the legacy default stream).  Buffers are caller-owned DEVICE pointers; no entry
+ *     point allocates device memory (the status word of clefq_status is a static
+ *     __device__ variable of the library).
+ *   - Calls that need scratch take a caller-provided `workspace` and have a
+ *     *_workspace_size query.
+ *   - Return value: CLEFQ_OK (0) or a negative clefq_status_t.  Shape checks mirror the
+ *     reference's `ensure!` conditions; clefq_last_error() describes the last failure of
+ *     the calling thread.
+ *   - Layouts are the reference's: BF16 as uint16 bit patterns; packed codes + scales in
+ *     one buffer (codes[rows][stride/P] u32, then f32 scales[rows]); weights in
+ *     128-row x 32-word tiles; routes/groups/order/tasks as f32 index buffers.
+ *   - Calls are reentrant on different streams.
+ *
+ * Reference citations are paths within the clef-hrx project.
+ */
+#ifndef CLEFQ_H
+#define CLEFQ_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CLEFQ_API __attribute__((visibility("default")))
+
+typedef enum {
+  CLEFQ_OK = 0,
+  CLEFQ_ERR_SHAPE = -1,   /* a shape/dtype/argument check failed (reference: ensure!) */
+  CLEFQ_ERR_ALIGN = -2,   /* a pointer or pitch is not 16-byte aligned */
+  CLEFQ_ERR_CUDA = -3,    /* a CUDA launch or runtime call failed */
+  CLEFQ_ERR_NCCL = -4,    /* a collective failed */
+  CLEFQ_ERR_TIMEOUT = -5, /* a bounded device-side wait gave up (see clefq_status) */
+  CLEFQ_ERR_WORKSPACE = -6 /* workspace missing or too small */
+} clefq_status_t;
+
+/* Packing pre-ops (src/quantized.rs:574-776; kernels/prepare_integer_register.loom). */
+typedef enum {
+  CLEFQ_PREP_PLAIN = 0,     /* h3_prepare_plain_tiled_i{4,8} */
+  CLEFQ_PREP_SWIGLU = 1,    /* h3_prepare_swiglu_i*: x = gate, aux = up (same shape) */
+  CLEFQ_PREP_ATTN_GATE = 2, /* h3_prepare_attention_gate_i*: aux = q_gate [rows][2*width] */
+  CLEFQ_PREP_NORM = 3,      /* h3_prepare_norm_i*: aux = RMSNorm weight [width], +1 offset, eps 1e-6 */
+  CLEFQ_PREP_NORM_STORE = 4 /* h3_prepare_norm_store_i*: also writes the BF16 normalized rows */
+} clefq_prep_kind_t;
+
+typedef enum { CLEFQ_BF16 = 0, CLEFQ_F32 = 1 } clefq_dtype_t;
+
+CLEFQ_API const char *clefq_last_error(void);
+CLEFQ_API int clefq_version(void);
+
+/*
+ * Synchronizes `stream`, then reads and clears this device's status word, which the
+ * tcgen05 kernels set when a bounded wait gives up.  Returns CLEFQ_OK or
+ * CLEFQ_ERR_TIMEOUT (or CLEFQ_ERR_CUDA if the stream itself failed).
+ */
+CLEFQ_API int clefq_status(void *stream);
+
+/*
+ * Rotate (Hadamard-256) and quantize rows; replaces prepare / prepare_with_source /
+ * prepare_with_inputs / prepare_attention_gate_with_source / prepare_norm*_with_source
+ * (src/quantized.rs:574-776) and their kernels (kernels/prepare_integer*.loom).
+ *   x        BF16 [rows][x_ld]          (width used)
+ *   aux      see clefq_prep_kind_t      (aux_ld in elements)
+ *   out      u32 codes[rows][stride/P] then f32 scales[rows]   (P = 32/bits)
+ *   operand  optional s8 GEMM operand [rows][operand_ld bytes] of the same codes
+ *            (bits 4 only; the tcgen05 GEMM's input format, 16*code, K-permuted)
+ *   norm_out BF16 [rows][norm_ld] normalized rows (CLEFQ_PREP_NORM_STORE only)
+ * Checks (src/quantized.rs:621-640): bits 4|8; 256 <= width <= 32768, width % 256 == 0;
+ * 1 <= rows <= 1048576; width <= stride <= 65536, stride % (512/bits) == 0.
+ * The RMSNorm pre-op accepts any width (the reference fixes 5120 and divides by 5120).
+ */
+CLEFQ_API int clefq_prepare(void *stream, int kind, int bits, const void *x, int64_t x_ld, const void *aux,
+                            int64_t aux_ld, int64_t rows, int64_t width, int64_t stride, void *out, void *operand,
+                            int64_t operand_ld, void *norm_out, int64_t norm_ld);
+
+/*
+ * Permute packed weight words into 128-row x 32-word blocks, dropping stride padding;
+ * replaces retile_codes (src/quantized.rs:542-572, kernels/retile_codes.loom).
+ *   codes u32 [rows][in_words] -> out u32 [rows * cols / (32/bits)] tiled.
+ * Checks: rows % 128 == 0, (cols/(32/bits)) % 32 == 0, in_words >= cols/(32/bits).
+ */
+CLEFQ_API int clefq_retile(void *stream, const void *codes, int64_t rows, int64_t cols, int bits, int64_t in_words,
+                           void *out);
+
+/*
+ * Dense quantized projection; replaces project_prepared + h3_gemm_i{4,8}_256[_residual]
+ * (src/quantized.rs:470-537, kernels/gemm_integer.loom:394-433):
+ *   y = (f32(sum_k a*w) * w_scales[n]) * a_scales[m] + 0
+ *   BF16 out: finite values saturate to +-3.3895e38; with residual: bf16(res + bf16(y)).
+ *   F32 out: y.
+ *   a_codes  packed codes [m][a_ld_words] (as written by clefq_prepare), a_scales f32 [m]
+ *   w_tiled  tiled codes of the [n][k] weight, w_scales f32 [n]
+ *   residual BF16 [m][residual_ld] or NULL (BF16 output only)
+ *   out      [m][out_ld] of out_dtype
+ * bits 4 needs workspace >= clefq_gemm_workspace_size(m, k, 4) (the s8 operand);
+ * bits 8 reads the packed codes directly (a_ld_words*4 must be a multiple of 16).
+ * Checks: n % 128 == 0, k % 256 == 0, k <= a_ld_words * (32/bits).
+ */
+CLEFQ_API int64_t clefq_gemm_workspace_size(int64_t m, int64_t k, int bits);
+CLEFQ_API int clefq_gemm(void *stream, int bits, const void *a_codes, int64_t a_ld_words, const float *a_scales,
+                         int64_t m, const void *w_tiled, const float *w_scales, int64_t n, int64_t k,
+                         const void *residual, int64_t residual_ld, int out_dtype, void *out, int64_t out_ld,
+                         void *workspace, int64_t workspace_bytes);
+/* Same projection from an s8 operand written by clefq_prepare (no unpack pass). */
+CLEFQ_API int clefq_gemm_s8(void *stream, int bits, const void *operand, int64_t operand_ld, const float *a_scales,
+                            int64_t m, const void *w_tiled, const float *w_scales, int64_t n, int64_t k,
+                            const void *residual, int64_t residual_ld, int out_dtype, void *out, int64_t out_ld);
+
+/* SwiGLU bf16(bf16(g/(1+exp(-g))) * u); replaces Engine::swiglu (src/ops.rs:9-29,
+ * kernels/swiglu.loom:41-50).  n elements, BF16. */
+CLEFQ_API int clefq_swiglu(void *stream, const void *gate, const void *up, int64_t n, void *out);
+
+/*
+ * Router; replaces omni_route (src/omni.rs:170-190, kernels/omni_route.loom:84-147):
+ * routes f32 [tokens][2*topk] = selected ids (as f32) || BF16-rounded probabilities.
+ * Checks: 0 < topk <= experts <= 128 and topk <= 32.  logits_dtype CLEFQ_BF16|CLEFQ_F32.
+ */
+CLEFQ_API int clefq_route(void *stream, const void *logits, int logits_dtype, int64_t tokens, int experts, int topk,
+                          float *routes);
+
+/*
+ * Stable grouping; replaces omni_group_routes / omni_group_routes_ordered
+ * (src/omni.rs:192-245, kernels/omni_group_routes{,_ordered}.loom):
+ *   groups f32 [experts][tokens+1] = count, then route ids t*topk+rank in token order
+ *   order  f32 [tokens][topk] (nullable) = rank of the j-th smallest expert id
+ * workspace >= clefq_group_workspace_size(tokens, topk, experts).
+ */
+CLEFQ_API int64_t clefq_group_workspace_size(int64_t tokens, int topk, int experts);
+CLEFQ_API int clefq_group_routes(void *stream, const float *routes, int64_t tokens, int topk, int experts,
+                                 float *groups, float *order, void *workspace, int64_t workspace_bytes);
+
+/* Task list [total, (expert, row0) per 16-row tile]; replaces omni_expert_tasks
+ * (src/omni.rs:126-169, kernels/omni_expert_tasks.loom:30-61). tasks f32 of length
+ * 1 + 2*(ceil(tokens*topk/16) + experts - 1). */
+CLEFQ_API int clefq_expert_tasks(void *stream, const float *groups, int64_t tokens, int experts, float *tasks);
+
+/*
+ * Grouped INT4 expert projection; replaces omni_expert_impl with groups
+ * (src/omni.rs:289-534; kernels/omni_expert_i4.loom, _compact, _k128_down):
+ *   for expert e, route r in groups[e]: x = input_routed ? r : r / topk
+ *   out[r][c] = bf16(f32(sum_k a[x][k] * w[e*n + c][k]) * (a_scales[x] * w_scales[e*n + c]))
+ *   a_codes packed int4 [rows][a_ld_words] + a_scales, rows = tokens (or tokens*topk routed)
+ *   w_tiled tiled [experts*n][k], w_scales [experts*n]; out BF16 [tokens*topk][n]
+ * Checks: n % 128 == 0 (the reference needs n % 256), k % 256 == 0.
+ * workspace >= clefq_expert_workspace_size(tokens, topk, experts, k).
+ */
+CLEFQ_API int64_t clefq_expert_workspace_size(int64_t tokens, int topk, int experts, int64_t k);
+CLEFQ_API int clefq_expert(void *stream, const void *a_codes, int64_t a_ld_words, const float *a_scales,
+                           const void *w_tiled, const float *w_scales, const float *groups, int64_t tokens, int topk,
+                           int experts, int64_t k, int64_t n, int input_routed, void *out, void *workspace,
+                           int64_t workspace_bytes);
+
+/*
+ * Weighted combine in ascending expert order with BF16 rounding at each step; replaces
+ * omni_combine_ordered (order != NULL) and omni_combine (order == NULL)
+ * (src/omni.rs:246-278,535-556; kernels/omni_combine{,_ordered}.loom).
+ *   values BF16 [tokens*topk][width], routes f32 [tokens][2*topk] -> out BF16 [tokens][width]
+ * Checks: width % 8 == 0.
+ */
+CLEFQ_API int clefq_combine(void *stream, const void *values, const float *routes, const float *order,
+                            int64_t tokens, int topk, int64_t width, void *out);
+
+/*
+ * Dense INT4 SwiGLU MLP block; replaces mlp() = project(gate), project(up),
+ * project_swiglu(gate, up, down, residual) (src/backbone.rs:880-894,
+ * src/quantized.rs:406-439), bit-identical to those separate steps:
+ *   prepare(x) -> gate, up projections -> SwiGLU -> prepare -> down projection (+ residual)
+ *   x BF16 [m][hidden]; gate/up tiled [inter][hidden] + scales; down tiled [hidden][inter]
+ *   out BF16 [m][hidden]; residual BF16 [m][hidden] or NULL
+ * workspace >= clefq_mlp_workspace_size(m, hidden, inter).
+ */
+CLEFQ_API int64_t clefq_mlp_workspace_size(int64_t m, int64_t hidden, int64_t inter);
+CLEFQ_API int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t inter, const void *gate_tiled,
+                        const float *gate_scales, const void *up_tiled, const float *up_scales, const void *down_tiled,
+                        const float *down_scales, const void *residual, void *out, void *workspace,
+                        int64_t workspace_bytes);
+
+/*
+ * Omni INT4 MoE block; replaces the expert part of forward_layers_cached
+ * (src/omni.rs:761-857, fast defaults): route(logits) -> ordered groups -> gate, up
+ * experts on the shared packed input -> SwiGLU -> down experts -> ordered combine.
+ *   x BF16 [tokens][hidden] (normalized input), logits [tokens][experts] (logits_dtype)
+ *   gate/up tiled [experts*inter][hidden] + scales; down tiled [experts*hidden][inter]
+ *   out BF16 [tokens][hidden]; routes_out f32 [tokens][2*topk] (nullable)
+ * workspace >= clefq_moe_workspace_size(tokens, hidden, inter, experts, topk).
+ */
+CLEFQ_API int64_t clefq_moe_workspace_size(int64_t tokens, int64_t hidden, int64_t inter, int experts, int topk);
+CLEFQ_API int clefq_moe(void *stream, const void *x, const void *logits, int logits_dtype, int64_t tokens,
+                        int64_t hidden, int64_t inter, int experts, int topk, const void *gate_tiled,
+                        const float *gate_scales, const void *up_tiled, const float *up_scales,
+                        const void *down_tiled, const float *down_scales, void *out, float *routes_out,
+                        void *workspace, int64_t workspace_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CLEFQ_H */

@@ -1,0 +1,331 @@
+"""GPU parity: the sm_100a kernels through the C ABI against the CPU oracle, bit for bit.
+
+Integer accumulators, codes, scales, routing ids, groupings and combine outputs are
+bit-exact; the BF16 epilogues are bit-exact too because both sides round identically and
+share one exp algorithm.  Every case runs twice on the device (replay determinism, as in
+the reference tests).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as o
+from tests.gpu_util import bf16_normal, from_dev_bf16, permuted_operand, same_bits_f32, to_dev, to_dev_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def cq():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import clefq
+    clefq.lib()
+    return clefq
+
+
+def _dev_prepared(cq, x_np, bits, stride, kind=0, aux=None):
+    x = to_dev_bf16(x_np)
+    a = None if aux is None else to_dev_bf16(aux)
+    return cq.prepare(x, bits, stride, kind, a)
+
+
+def _words(p):
+    return p.codes.cpu().numpy().view(np.uint32)
+
+
+# ---------------------------------------------------------------------------------------
+# packing
+# ---------------------------------------------------------------------------------------
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("width", [256, 768, 1280, 5120, 6144, 8192, 17408])
+def test_prepare_matches_golden(cq, golden, bits, width):
+    key = f"pack_b{bits}_w{width}"
+    x = golden[key + "_x"]
+    stride = width + 512 // bits
+    for _ in range(2):
+        p = _dev_prepared(cq, x, bits, stride)
+        words = _words(p)
+        assert np.array_equal(words[:, : width // (32 // bits)], golden[key + "_words"])
+        assert not np.any(words[:, width // (32 // bits):]), "stride padding must be zero"
+        _, _, oscales, _ = o.prepare(x, bits, stride)
+        assert same_bits_f32(p.scales.cpu().numpy(), oscales)
+        if bits == 4:
+            assert np.array_equal(p.operand.cpu().numpy(), permuted_operand(words, width))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_prepare_exceptional_rows(cq, golden, bits):
+    x = golden[f"exc_b{bits}_x"]
+    p = _dev_prepared(cq, x, bits, 5120 + 512 // bits)
+    assert np.array_equal(_words(p)[:, : 5120 // (32 // bits)], golden[f"exc_b{bits}_words"])
+    assert same_bits_f32(p.scales.cpu().numpy(), golden[f"exc_b{bits}_scales"])
+
+
+@pytest.mark.parametrize("rows,width", [(1, 256), (7, 768), (33, 2048), (130, 4096), (5, 12288), (3, 32768)])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_prepare_random_matches_oracle(cq, rows, width, bits):
+    rng = np.random.default_rng(rows * 7 + width)
+    x = bf16_normal(rng, (rows, width))
+    stride = o.stride_for(width, bits)
+    p = _dev_prepared(cq, x, bits, stride)
+    storage, _, _, _ = o.prepare(x, bits, stride)
+    assert np.array_equal(p.storage.cpu().numpy().view(np.uint32), storage)
+
+
+def _gate_like(rng, rows, width):
+    """SwiGLU/attention gate inputs with the reference test's exceptional rows
+    (src/quantized.rs:1187-1266): 0, NaN, Inf, bf16 MAX, subnormal, +-80, formula."""
+    i = np.arange(rows * width)
+    col = i % width
+    kind = (i // width) % 7
+    v = ((i * 17 % 1031).astype(np.float32) - 515) / 16
+    v = np.where(kind == 0, 0.0, v)
+    v = np.where((kind == 1) & (col == 259), np.nan, v)
+    v = np.where((kind == 2) & (col == 515), np.inf, v)
+    v = np.where(kind == 3, o.bf16_to_f32(np.uint16(0x7F7F)), v)
+    v = np.where(kind == 4, np.uint32(0x00010000).view(np.float32), v)
+    v = np.where(kind == 5, np.where(col % 2 == 0, -80.0, 80.0), v)
+    return o.f32_to_bf16(v.astype(np.float32)).reshape(rows, width)
+
+
+@pytest.mark.parametrize("rows,width", [(9, 768), (14, 17408), (130, 2048)])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_fused_swiglu_packing(cq, rows, width, bits):
+    """Fused SwiGLU packing == oracle, and == the separate swiglu op + prepare
+    (src/quantized.rs:1187-1266)."""
+    rng = np.random.default_rng(width)
+    g = _gate_like(rng, rows, width)
+    i = np.arange(rows * width)
+    u = o.f32_to_bf16(((i * 29 % 997).astype(np.float32) - 498) / 32).reshape(rows, width)
+    stride = width + 512 // bits
+    fused = _dev_prepared(cq, g, bits, stride, cq.PREP_SWIGLU, u)
+    storage, _, _, _ = o.prepare(g, bits, stride, o.SWIGLU, u)
+    assert np.array_equal(fused.storage.cpu().numpy().view(np.uint32), storage)
+    act = cq.swiglu(to_dev_bf16(g), to_dev_bf16(u))
+    assert np.array_equal(from_dev_bf16(act), o.swiglu(g, u))
+    sep = cq.prepare(act, bits, stride)
+    assert torch.equal(sep.storage, fused.storage)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("rows", [1, 158])
+def test_attention_gate_packing(cq, bits, rows):
+    """src/quantized.rs:1268-1368: Q halves are poisoned with NaN and must be ignored."""
+    width = 6144
+    rng = np.random.default_rng(rows)
+    att = bf16_normal(rng, (rows, width), 4.0)
+    q = _gate_like(rng, rows, 2 * width).copy()
+    colq = np.arange(2 * width)
+    q[:, (colq % 512) < 256] = 0x7FC0
+    stride = width + 512 // bits
+    p = _dev_prepared(cq, att, bits, stride, cq.PREP_ATTN_GATE, q)
+    storage, _, _, _ = o.prepare(att, bits, stride, o.ATTN_GATE, q)
+    assert np.array_equal(p.storage.cpu().numpy().view(np.uint32), storage)
+
+
+@pytest.mark.parametrize("width", [5120, 2560])
+def test_norm_packing(cq, width):
+    rng = np.random.default_rng(width)
+    rows = 37
+    x = bf16_normal(rng, (rows, width), 3.0)
+    w = bf16_normal(rng, (width,), 0.02)
+    stride = o.stride_for(width)
+    for kind, okind in ((cq.PREP_NORM, o.NORM), (cq.PREP_NORM_STORE, o.NORM_STORE)):
+        p = _dev_prepared(cq, x, 4, stride, kind, w)
+        storage, _, _, norm = o.prepare(x, 4, stride, okind, w)
+        assert np.array_equal(p.storage.cpu().numpy().view(np.uint32), storage)
+        if norm is not None:
+            assert np.array_equal(from_dev_bf16(p.norm), norm)
+
+
+@pytest.mark.parametrize("bits,rows,cols,padded", [(4, 256, 1024, True), (4, 384, 512, False),
+                                                  (8, 128, 256, False), (4, 768, 2048, True)])
+def test_retile(cq, bits, rows, cols, padded):
+    stride = cols + (512 // bits if padded else 0)
+    in_words = stride // (32 // bits)
+    vals = (np.arange(rows * in_words, dtype=np.uint64) * 2654435761 % (1 << 32)).astype(np.uint32)
+    vals = vals.reshape(rows, in_words)
+    out = cq.retile_codes(to_dev(vals.view(np.int32)), rows, cols, bits)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), o.retile(vals, rows, cols, bits))
+
+
+# ---------------------------------------------------------------------------------------
+# dense GEMM
+# ---------------------------------------------------------------------------------------
+def _weight(rng, n, k, bits=4):
+    w = bf16_normal(rng, (n, k), 0.05)
+    wt, ws = o.pack_weight(w, bits)
+    dev = cq_weight(wt, ws, n, k, bits)
+    return w, wt, ws, dev
+
+
+def cq_weight(wt, ws, n, k, bits):
+    import clefq
+    return clefq.QuantizedWeight(to_dev(wt.view(np.int32)), to_dev(ws), n, k, o.stride_for(k, bits), bits)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 128, 256), (17, 256, 512), (127, 128, 2048), (128, 768, 2048),
+                                   (129, 384, 1024), (300, 256, 4096), (64, 128, 12288)])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_gemm_matches_oracle(cq, m, n, k, bits):
+    rng = np.random.default_rng(m * 131 + n + k)
+    _, wt, ws, wdev = _weight(rng, n, k, bits)
+    x = bf16_normal(rng, (m, k))
+    stride = o.stride_for(k, bits)
+    _, ocodes, oscales, _ = o.prepare(x, bits, stride)
+    ref, acc = o.gemm(ocodes, oscales, wt, ws, n, k, bits=bits, want_acc=True)
+    ref32 = o.gemm(ocodes, oscales, wt, ws, n, k, bits=bits, out_f32=True)
+    a = cq.prepare(to_dev_bf16(x), bits, stride)
+    for _ in range(2):
+        out = cq.project_prepared(m, wdev, a)          # s8 operand path (bits 4) / in-place (bits 8)
+        assert np.array_equal(from_dev_bf16(out), ref)
+    a_packed = cq.Prepared(a.storage, a.codes, a.scales, None, None, bits, stride)
+    out2 = cq.project_prepared(m, wdev, a_packed)        # packed-codes path (unpack into workspace)
+    assert np.array_equal(from_dev_bf16(out2), ref)
+    out32 = cq.project_prepared(m, wdev, a, out_dtype=torch.float32)
+    assert same_bits_f32(out32.cpu().numpy(), ref32)
+
+
+@pytest.mark.parametrize("m", [1, 127, 256])
+def test_gemm_residual(cq, m):
+    """h3_gemm_i4_256_residual: bf16(res + bf16(y)), incl. NaN/Inf residuals and 1e34 scales
+    (src/quantized.rs:1409-1552)."""
+    rng = np.random.default_rng(m)
+    n, k = 256, 1024
+    _, wt, ws, wdev = _weight(rng, n, k)
+    x = bf16_normal(rng, (m, k))
+    res = bf16_normal(rng, (m, n))
+    res[0, 0] = 0x7FC0
+    res[0, 1] = 0x7F80
+    x[0, :] = o.f32_to_bf16(np.full(k, 1e34, np.float32))
+    stride = o.stride_for(k)
+    _, ocodes, oscales, _ = o.prepare(x, 4, stride)
+    ref = o.gemm(ocodes, oscales, wt, ws, n, k, residual=res)
+    out = cq.project_quantized(to_dev_bf16(x), wdev, residual=to_dev_bf16(res))
+    got = from_dev_bf16(out)
+    nan_ref = np.isnan(o.bf16_to_f32(ref))
+    assert np.array_equal(np.isnan(o.bf16_to_f32(got)), nan_ref)
+    assert np.array_equal(got[~nan_ref], ref[~nan_ref])
+
+
+def test_mlp_block(cq):
+    """Dense SwiGLU MLP block through one C-ABI call, bit-exact to the oracle's separate
+    steps (prepare, gate, up, swiglu, prepare, down)."""
+    rng = np.random.default_rng(5)
+    m, h, inter = 200, 1024, 768
+    ws = []
+    for n, k in ((inter, h), (inter, h), (h, inter)):
+        _, wt, s, dev = _weight(rng, n, k)
+        ws.append(((wt, s, n), dev))
+    x = bf16_normal(rng, (m, h))
+    ref = o.mlp_block(x, ws[0][0], ws[1][0], ws[2][0])
+    for _ in range(2):
+        out = cq.mlp(to_dev_bf16(x), ws[0][1], ws[1][1], ws[2][1])
+        assert np.array_equal(from_dev_bf16(out), ref)
+    cq.status()
+
+
+# ---------------------------------------------------------------------------------------
+# MoE operators
+# ---------------------------------------------------------------------------------------
+@pytest.mark.parametrize("experts,topk", [(128, 8), (64, 8), (128, 4)])
+@pytest.mark.parametrize("phase", [0, 1, 2, 3])
+@pytest.mark.parametrize("bf", [0, 1])
+def test_route(cq, golden, experts, topk, phase, bf):
+    key = f"route_e{experts}_k{topk}_p{phase}_bf{bf}"
+    logits = golden[key + "_logits"]
+    ref = o.route(logits, topk)
+    dev = to_dev_bf16(logits) if bf else to_dev(logits)
+    out = cq.omni_route(dev, topk).cpu().numpy()
+    assert np.array_equal(out[:, :topk], golden[key + "_ids"])
+    assert same_bits_f32(out, ref)
+
+
+def test_route_random_large(cq):
+    rng = np.random.default_rng(11)
+    logits = bf16_normal(rng, (4099, 128))
+    ref = o.route(logits, 8)
+    out = cq.omni_route(to_dev_bf16(logits), 8).cpu().numpy()
+    assert same_bits_f32(out, ref)
+
+
+@pytest.mark.parametrize("tokens", [1, 17, 64, 65, 255, 256, 2048, 5000])
+@pytest.mark.parametrize("phase", [0, 1, 2])
+def test_group_order_tasks(cq, tokens, phase):
+    from tests.golden.make_golden import expert_routes
+    routes = expert_routes(tokens, phase == 1, phase)
+    g_ref, o_ref = o.group(routes)
+    groups, order = cq.omni_group_routes_ordered(to_dev(routes))
+    g = groups.cpu().numpy()
+    for e in range(128):
+        n = int(g_ref[e, 0])
+        assert np.array_equal(g[e, : n + 1], g_ref[e, : n + 1])
+    assert np.array_equal(order.cpu().numpy(), o_ref)
+    tasks = cq.omni_expert_tasks(groups, tokens).cpu().numpy()
+    t_ref = o.tasks(g_ref, tokens)
+    total = int(t_ref[0])
+    assert np.array_equal(tasks[: 1 + 2 * total], t_ref[: 1 + 2 * total])
+
+
+def _expert_weights(rng, experts, n, k):
+    w = bf16_normal(rng, (experts * n, k), 0.05)
+    wt, ws = o.pack_weight(w)
+    return wt, ws, cq_weight(wt, ws, experts * n, k, 4)
+
+
+@pytest.mark.parametrize("tokens,skewed", [(1, False), (37, False), (300, True), (1000, False)])
+@pytest.mark.parametrize("routed", [False, True])
+def test_expert_matches_oracle(cq, tokens, skewed, routed):
+    """Grouped INT4 experts, bit-exact (src/benchmarking/omni.rs:176-345 fixtures)."""
+    from tests.golden.make_golden import expert_routes
+    rng = np.random.default_rng(tokens)
+    experts, topk = 128, 8
+    k, n = (256, 512) if routed else (512, 256)
+    wt, ws, wdev = _expert_weights(rng, experts, n, k)
+    routes = expert_routes(tokens, skewed, 0)
+    groups, _ = o.group(routes)
+    rows = tokens * topk if routed else tokens
+    i = np.arange(rows * k)
+    x = o.f32_to_bf16(((i * 17) % 251).astype(np.float32) / 128 - 1).reshape(rows, k)
+    _, xc, xs, _ = o.prepare(x, 4, o.stride_for(k))
+    ref = o.expert(xc, xs, wt, ws, groups, tokens, k, n, routed)
+    a = cq.prepare(to_dev_bf16(x), 4, o.stride_for(k))
+    for _ in range(2):
+        out = cq.omni_expert(a, to_dev(routes), to_dev(groups), wdev, routed)
+        assert np.array_equal(from_dev_bf16(out), ref)
+
+
+@pytest.mark.parametrize("ordered", [True, False])
+@pytest.mark.parametrize("tokens", [1, 37, 513])
+def test_combine(cq, ordered, tokens):
+    from tests.golden.make_golden import expert_routes
+    rng = np.random.default_rng(tokens)
+    width = 2048
+    routes = expert_routes(tokens, False, 1)
+    routes[:, 8:] = o.bf16_to_f32(o.f32_to_bf16(rng.random((tokens, 8)).astype(np.float32)))
+    values = bf16_normal(rng, (tokens * 8, width))
+    _, order = o.group(routes)
+    ref = o.combine(values, routes, order if ordered else None)
+    out = cq.omni_combine_ordered(to_dev_bf16(values), to_dev(routes), to_dev(order) if ordered else None)
+    assert np.array_equal(from_dev_bf16(out), ref)
+
+
+@pytest.mark.parametrize("tokens", [300, 1024])
+def test_moe_block(cq, tokens):
+    """The fused MoE block (route -> groups -> gate|up -> SwiGLU packing -> down -> combine)
+    equals the oracle's separate reference operators bit for bit."""
+    rng = np.random.default_rng(tokens)
+    experts, topk, hidden, inter = 128, 8, 512, 256
+    gt, gs, gdev = _expert_weights(rng, experts, inter, hidden)
+    ut, us, udev = _expert_weights(rng, experts, inter, hidden)
+    dt, ds, ddev = _expert_weights(rng, experts, hidden, inter)
+    x = bf16_normal(rng, (tokens, hidden))
+    logits = bf16_normal(rng, (tokens, experts))
+    ref, ref_routes, _, _ = o.moe_layer(x, logits, (gt, gs, inter), (ut, us, inter), (dt, ds, hidden))
+    routes_out = torch.empty((tokens, 2 * topk), dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        out = cq.omni_moe(to_dev_bf16(x), to_dev_bf16(logits), gdev, udev, ddev, routes_out=routes_out)
+        assert same_bits_f32(routes_out.cpu().numpy(), ref_routes)
+        assert np.array_equal(from_dev_bf16(out), ref)
+    cq.status()
