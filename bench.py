@@ -1,0 +1,385 @@
+"""Benchmark of the INT4 MLP/MoE prefill path on B200 (driver contract: one JSON line).
+
+Headline workload ("C2"): the dense INT4 SwiGLU MLP block, 4096
+tokens, hidden 4096, intermediate 12288 -- prepare(x) -> gate|up GEMM -> fused SwiGLU
+packing -> down GEMM, one clefq_mlp C-ABI call per step.  Synthetic data (seed 0 + rank):
+activations BF16 N(0,1), weight codes uniform in [-8, 7] (uniform random tiled words),
+one f32 scale per output row |N(0, 0.02)|/7.  The L2 (126 MB) is flushed by a 256 MB
+write between timed steps; each step is timed with CUDA events on the launching stream.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl clefq|reference]
+
+Multi-GPU: one process per GPU (torchrun); every rank runs its own 4096-token block with
+replicated weights (data-parallel replicas, no collective on the data path): weak scaling.
+--impl reference: the reference's CPU semantics (the C/OpenMP oracle port; the reference
+itself is Rust + hrx-rs on an AMD gfx1151 and cannot run here) on the host cores, rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "INT4 MLP/MoE prefill tokens/s"
+M, HIDDEN, INTER = 4096, 4096, 12288          # C2
+MOE_T, MOE_H, MOE_I, MOE_E, MOE_K = 8192, 2048, 768, 128, 8   # C4
+FLUSH_BYTES = 256 << 20
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p.get("hbm_gbs", 6650.0), p.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def load_traffic():
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(power) if power else None, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def all_max(world, value: float) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------------------
+# synthetic weights (BASELINE: codes uniform in [-8, 7], scales |N(0, 0.02)|/7)
+# ---------------------------------------------------------------------------------------
+def rand_weight_dev(clefq, rows, cols, gen):
+    codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (rows * cols // 8,), dtype=torch.int32, device="cuda", generator=gen)
+    scales = (torch.randn(rows, device="cuda", generator=gen).abs() * 0.02 / 7).float()
+    return clefq.QuantizedWeight(codes, scales, rows, cols, clefq.stride_for(cols), 4)
+
+
+def rand_weight_host(rng, rows, cols):
+    codes = rng.integers(0, 2 ** 32, size=rows * cols // 8, dtype=np.uint64).astype(np.uint32)
+    scales = (np.abs(rng.standard_normal(rows)) * 0.02 / 7).astype(np.float32)
+    return codes, scales, rows
+
+
+def time_steps(fn, steps, flush):
+    """Device time of each step (CUDA events on the launching stream), L2 flushed before
+    every step; returns per-step milliseconds."""
+    stream = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        flush.fill_(1)
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+# ---------------------------------------------------------------------------------------
+# CPU legs (oracle port): only here, the tests and smoke() may run oracle/
+# ---------------------------------------------------------------------------------------
+def cpu_mlp_sample(tokens: int, min_seconds: float, threads: int):
+    from oracle import oracle as o
+    rng = np.random.default_rng(0)
+    g, u, d = rand_weight_host(rng, INTER, HIDDEN), rand_weight_host(rng, INTER, HIDDEN), rand_weight_host(rng, HIDDEN, INTER)
+    x = o.f32_to_bf16(rng.standard_normal((tokens, HIDDEN)).astype(np.float32))
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        o.mlp_block(x, g, u, d, threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds and reps >= 2:
+            break
+    return tokens * reps / el, reps, el
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    threads = len(os.sched_getaffinity(0))
+    from oracle import oracle as o
+    rng = np.random.default_rng(0)
+    g, u, d = rand_weight_host(rng, INTER, HIDDEN), rand_weight_host(rng, INTER, HIDDEN), rand_weight_host(rng, HIDDEN, INTER)
+    sample = 256
+    x = o.f32_to_bf16(rng.standard_normal((sample, HIDDEN)).astype(np.float32))
+    for _ in range(args.warmup):
+        o.mlp_block(x, g, u, d, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        o.mlp_block(x, g, u, d, threads=threads)
+        times.append(time.perf_counter() - t0)
+    ms = 1000 * sum(times) / len(times)
+    value = sample / (ms / 1000)
+    desc = (f"{sample} of the 4096 C2 tokens per step through the full-size weights "
+            f"(hidden {HIDDEN}, intermediate {INTER}), oracle port of the reference semantics")
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4 codes, int32 dot, f32 epilogue", "data": "synthetic (seed 0)",
+            "impl": "reference",
+            "config": {"workload": "C2 dense INT4 SwiGLU MLP block (CPU sample)", "tokens_per_step": sample,
+                       "hidden": HIDDEN, "intermediate": INTER, "parallelism": "host cores"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------
+def run_clefq(args, world, rank, local):
+    import clefq
+    clefq.lib()
+    hbm_peak, bf16_peak, peak_kind = load_peaks()
+    i8_peak = 2 * bf16_peak   # B200: dense int8 tensor rate is twice dense bf16
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1000 + rank)
+    gate, up, down = (rand_weight_dev(clefq, INTER, HIDDEN, gen), rand_weight_dev(clefq, INTER, HIDDEN, gen),
+                      rand_weight_dev(clefq, HIDDEN, INTER, gen))
+    x = torch.randn(M, HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
+    ws = torch.empty(clefq.lib().clefq_mlp_workspace_size(M, HIDDEN, INTER), dtype=torch.uint8, device="cuda")
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    step = lambda: clefq.mlp(x, gate, up, down, workspace=ws)   # noqa: E731
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    # W warm-up steps at least; keep warming for ~1 s so the clock samples see the load.
+    t0, done = time.perf_counter(), 0
+    while done < args.warmup or time.perf_counter() - t0 < 1.0:
+        step()
+        done += 1
+        if done % 50 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    clefq.status()
+    barrier(world)
+    torch.cuda.synchronize()
+    times = time_steps(step, args.steps, flush)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    clefq.status()
+    ms_local = sum(times) / len(times)
+    ms = all_max(world, ms_local)
+    value = world * M / (ms / 1000)
+
+    # ---- per-kernel timing of the same step (dominant kernel: the gate|up GEMM) -------
+    a = clefq.prepare(x, 4, clefq.stride_for(HIDDEN))
+    gu = torch.zeros((M, 2 * INTER), dtype=torch.bfloat16, device="cuda")
+    ktimes = {}
+    reps = max(5, min(args.steps, 50))
+
+    def gemm_gu():
+        clefq._call("clefq_gemm_s8", clefq._stream(), 4, clefq._ptr(a.operand), HIDDEN, clefq._ptr(a.scales), M,
+                    clefq._ptr(gate.codes), clefq._ptr(gate.scales), INTER, HIDDEN, None, 0, 0, clefq._ptr(gu),
+                    2 * INTER)
+    hid = clefq.prepare(gu[:, :INTER], 4, INTER + (128 if INTER % 1024 == 0 else 0), clefq.PREP_SWIGLU, gu[:, INTER:])
+    out = torch.empty((M, HIDDEN), dtype=torch.bfloat16, device="cuda")
+
+    def gemm_down():
+        clefq._call("clefq_gemm_s8", clefq._stream(), 4, clefq._ptr(hid.operand), INTER, clefq._ptr(hid.scales), M,
+                    clefq._ptr(down.codes), clefq._ptr(down.scales), HIDDEN, INTER, None, 0, 0, clefq._ptr(out),
+                    HIDDEN)
+    for name, fn in (("gemm_gate", gemm_gu), ("gemm_down", gemm_down)):
+        fn()
+        ktimes[name] = statistics.median(time_steps(fn, reps, flush))
+    ktimes["prepare_x"] = statistics.median(time_steps(lambda: clefq.prepare(x, 4, clefq.stride_for(HIDDEN)), reps,
+                                                       flush))
+    # gate|up run as one launch inside the step (2*INTER output columns); the separate
+    # gate-only GEMM above has the same per-tile work, so ops scale with its N.
+    gemm_ops = 2.0 * M * INTER * HIDDEN
+    achieved = gemm_ops / (ktimes["gemm_gate"] / 1000) / 1e12
+    traffic = load_traffic().get("gemm_c2_gate", None)
+
+    # ---- end to end through the public API with host buffers ---------------------------
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((M, HIDDEN), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = clefq.mlp(x_dev, gate, up, down, workspace=ws)
+        out_host.copy_(y, non_blocking=True)
+    e2e_step()
+    torch.cuda.synchronize()
+    e2e_times = time_steps(e2e_step, max(5, min(args.steps, 50)), flush)
+    e2e_ms = all_max(world, sum(e2e_times) / len(e2e_times))
+
+    # ---- secondary workload: the C4 MoE layer (8192 tokens, 128 experts, top-8) --------
+    moe = None
+    if not args.skip_moe:
+        mg = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
+        mu = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
+        md = rand_weight_dev(clefq, MOE_E * MOE_H, MOE_I, gen)
+        mx = torch.randn(MOE_T, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
+        wr = torch.randn(MOE_E, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
+        logits = mx @ wr.t()     # router linear (BF16, cuBLAS): outside the INT4 path
+        mws = torch.empty(clefq.lib().clefq_moe_workspace_size(MOE_T, MOE_H, MOE_I, MOE_E, MOE_K), dtype=torch.uint8,
+                          device="cuda")
+        mstep = lambda: clefq.omni_moe(mx, logits, mg, mu, md, workspace=mws)   # noqa: E731
+        for _ in range(3):
+            mstep()
+        torch.cuda.synchronize()
+        clefq.status()
+        mt = time_steps(mstep, max(5, min(args.steps, 30)), flush)
+        mms = all_max(world, sum(mt) / len(mt))
+        ops = 2.0 * MOE_T * MOE_K * (MOE_H * 2 * MOE_I + MOE_I * MOE_H)
+        moe = {"workload": "C4 Omni INT4 MoE layer: 8192 tokens, hidden 2048, 128 experts x (gate|up 2048->2x768, "
+                           "down 768->2048), top-8", "tokens_per_s": world * MOE_T / (mms / 1000), "ms_per_step": mms,
+               "tops": ops / (mms / 1000) / 1e12, "frac_of_int8_peak": ops / (mms / 1000) / 1e12 / i8_peak}
+
+    launches = 4 * args.steps
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4 x int4 -> int32 (tcgen05 kind::i8), f32 epilogue, bf16 activations",
+        "data": "synthetic (seed 1000+rank): x bf16 N(0,1), codes uniform [-8,7], scales |N(0,0.02)|/7",
+        "config": {"workload": "C2 dense INT4 SwiGLU MLP block", "tokens_per_gpu": M, "hidden": HIDDEN,
+                   "intermediate": INTER, "parallelism": f"dp{world} (replicas)" if world > 1 else "single GPU",
+                   "l2": "flushed (256 MB write) before every timed step"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_i8_kernel (gate GEMM 4096x12288x4096)",
+                     "achieved": achieved, "peak": i8_peak, "unit": "TOP/s", "frac": achieved / i8_peak,
+                     "traffic": traffic,
+                     "peak_note": f"kind::i8 dense = 2 x {peak_kind} bf16 burst ({bf16_peak} TF/s) from "
+                                  "MEASURED_PEAKS.json"},
+        "kernels_ms": ktimes,
+        "e2e": {"value": world * M / (e2e_ms / 1000), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(M * HIDDEN * 2)},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if moe:
+        line["secondary"] = moe
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        threads = len(os.sched_getaffinity(0))
+        cpu_val, reps, el = cpu_mlp_sample(512, 10.0, threads)
+        line["cpu_baseline"] = {"value": cpu_val, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": f"{reps} x 512 of the C2 tokens through the full-size weights "
+                                          f"({el:.1f} s), CPU oracle port (OpenMP, AVX-512 VNNI dot)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="clefq", choices=["clefq", "reference"])
+    ap.add_argument("--skip-moe", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        # The reference arm runs on the host cores of rank 0; other ranks exit without work.
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), 0)
+        return
+    world, rank, local = dist_init()
+    try:
+        run_clefq(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -383,6 +383,7 @@ int clefq_expert(void *stream, const void *a_codes, int64_t a_ld_words, const fl
   p.expert_offsets = offsets;
   p.perm = perm;
   p.max_tiles = (int)((routes + 127) / 128 + experts);
+  p.experts = experts;
   p.topk = topk;
   p.scale_mode = input_routed ? 2 : 1;
   p.scatter = 1;
@@ -530,6 +531,7 @@ int clefq_moe(void *stream, const void *x, const void *logits, int logits_dtype,
   p.expert_offsets = t.offsets;
   p.perm = t.perm;
   p.max_tiles = (int)((nroutes + 127) / 128 + experts);
+  p.experts = experts;
   p.topk = topk;
   p.scale_mode = 1;  // activation scale of the token
   p.scatter = 0;     // rows stay in expert-sorted order

@@ -56,6 +56,7 @@ struct GemmParams {
   const int *expert_offsets;// [experts + 1] sorted-row offsets
   const int *perm;          // sorted position -> route id
   int max_tiles;
+  int experts;              // experts whose weights are stacked in w[] (grouped)
   int topk;
   int scale_mode;           // a_scales index: 0 -> p, 1 -> perm[p] / topk, 2 -> perm[p]
   int scatter;              // output row: 1 -> perm[p], 0 -> p

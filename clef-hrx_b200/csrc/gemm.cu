@@ -32,96 +32,98 @@ namespace {
 
 constexpr int BM = 128;                       // weight rows per tile (MMA M)
 constexpr int BN = 128;                       // tokens per tile (MMA N)
-constexpr int KB = 256;                       // codes per K block
-constexpr int NS = 3;                         // token ring stages (KB bytes x BN rows each)
-constexpr int STAGE_BYTES = BN * KB;          // 32 KiB
-constexpr int TMEM_COLS = 256;                // acc 128 + two 64-column weight stages
-constexpr int ACC_COL = 0;
-constexpr int WCOL0 = 128;
-constexpr int THREADS = 192;
+constexpr int KS = 128;                       // codes per pipeline stage
+constexpr int TOK_BYTES = BN * KS;            // 16 KiB: one 128-byte-swizzled TMA box
+constexpr int TMEM_COLS = 512;                // 2 accumulators x 128 + weight stages x 32
+constexpr int WCOL0 = 256;
+constexpr int THREADS = 448;                  // 8 converter, 1 TMA, 1 MMA, 4 epilogue warps
+constexpr int CONV_WARPS = 8;                 // two groups of 4: even and odd stages
+constexpr int TMA_WARP = 8, MMA_WARP = 9;
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
-constexpr int SMEM_BYTES = NS * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 
+constexpr int STAGING_BYTES = BN * BM * 2;    // one BF16 output tile [token][column]
+
+template <int BITS>
+struct Cfg {
+  static constexpr int NS = BITS == 4 ? 8 : 6;           // ring depth
+  static constexpr int W_BYTES = BM * KS * BITS / 8;     // packed weight bytes per stage
+  static constexpr int STAGE = TOK_BYTES + W_BYTES;
+  static constexpr int SMEM = NS * STAGE + STAGING_BYTES + 1024 + 512;
+};
+
+template <int NS>
 struct Smem {
-  uint64_t tok_full[NS], tok_empty[NS], w_full[2], w_empty[2], acc_full;
+  uint64_t tok_full[NS], tok_empty[NS], wsm_full[NS], wsm_empty[NS], wtm_full[NS], wtm_empty[NS];
+  uint64_t acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int err;
 };
 
-// One K=256 block of a weight row (32 packed int4 words) -> 64 TMEM columns of s8
-// (16 * code, K-permuted like the token operand), stored as two 32-column halves.
-CQ_DEV void store_block_i4(const uint32_t (&w)[32], uint32_t taddr) {
-  uint32_t o[32];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        o[8 * g + i] = nib_lo16(w[16 * h + 4 * g + i]);
-        o[8 * g + 4 + i] = nib_hi16(w[16 * h + 4 * g + i]);
-      }
+// Tile t of this launch -> (token tile row, output column tile, expert); false past the end.
+struct TileMap {
+  int n_tiles, total;
+  CQ_DEV bool get(const GemmParams &p, int t, int64_t &row0, int &rows_valid, int &n_tile, int &expert) const {
+    if (t >= total) return false;
+    const int mt = t / n_tiles;
+    n_tile = t - mt * n_tiles;
+    if (p.grouped) {
+      expert = p.tile_list[1 + 2 * mt];
+      row0 = p.tile_list[2 + 2 * mt];
+      const int64_t end = p.expert_offsets[expert + 1];
+      rows_valid = (int)(end - row0 < BN ? end - row0 : BN);
+    } else {
+      expert = 0;
+      row0 = (int64_t)mt * BN;
+      rows_valid = (int)(p.m - row0 < BN ? p.m - row0 : BN);
     }
-    tmem_st_x32(taddr + 32 * h, o);
+    return true;
   }
-}
+};
 
-CQ_DEV void load_words(uint32_t (&w)[32], const uint32_t *src) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    uint4 v = ldg_nc_v4(src + 4 * i);
-    w[4 * i] = v.x;
-    w[4 * i + 1] = v.y;
-    w[4 * i + 2] = v.z;
-    w[4 * i + 3] = v.w;
-  }
-}
-
-template <bool GROUPED>
-__global__ void __launch_bounds__(THREADS, 2) gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap, GemmParams p) {
+// Persistent: one CTA per SM walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+// Pipelines (all indexed by a stage counter g that runs across tiles):
+//   TMA warp   -> tokens + packed weights into ring slot g % NS
+//   converters -> weight slot: swizzled smem -> s8 (16*code) -> TMEM weight stage g % NS;
+//                 two groups of four warps take alternate stages
+//   MMA thread -> 4 x tcgen05.mma (K=32 each) into accumulator (tile & 1)
+//   epilogue   -> drains accumulator (tile & 1) while the next tile accumulates in the other
+template <bool GROUPED, int BITS>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tok_map, const __grid_constant__ CUtensorMap w_map0,
+                   const __grid_constant__ CUtensorMap w_map1, GemmParams p) {
+  using C = Cfg<BITS>;
+  constexpr int NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t *ring = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  Smem &s = *reinterpret_cast<Smem *>(ring + NS * STAGE_BYTES);
+  uint16_t *staging = reinterpret_cast<uint16_t *>(ring + NS * C::STAGE);
+  Smem<NS> &s = *reinterpret_cast<Smem<NS> *>(ring + NS * C::STAGE + STAGING_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // ---- tile coordinates ------------------------------------------------------------
-  int n_tile = blockIdx.x;                 // weight-row tile
-  int64_t row0;                            // first operand row of the token tile
-  int rows_valid;                          // token rows of this tile that are real
-  int expert = 0;
-  if (GROUPED) {
-    const int ntiles = p.tile_list[0];
-    if ((int)blockIdx.y >= ntiles) return;
-    expert = p.tile_list[1 + 2 * blockIdx.y];
-    row0 = p.tile_list[2 + 2 * blockIdx.y];
-    const int64_t end = p.expert_offsets[expert + 1];
-    rows_valid = (int)(end - row0 < BN ? end - row0 : BN);
-  } else {
-    row0 = (int64_t)blockIdx.y * BN;
-    rows_valid = (int)(p.m - row0 < BN ? p.m - row0 : BN);
-  }
-  const int k_blocks = p.k / KB;
-  const int words_per_row_block = 32;                       // 128 bytes of one tiled row
-  const int64_t blocks_k = (int64_t)p.k / (32 * (32 / p.bits));
-  const int which = n_tile / p.n_split;                    // weight matrix feeding this tile
-  const int local_tile = n_tile - which * p.n_split;
-  const int64_t w_row_tile = (int64_t)expert * p.n_split + local_tile;
+  TileMap tm;
+  tm.n_tiles = p.n / BM;
+  tm.total = (GROUPED ? p.tile_list[0] : (int)((p.m + BN - 1) / BN)) * tm.n_tiles;
+  if ((int)blockIdx.x >= tm.total) return;
+  const int k_stages = p.k / KS;
+  const int blocks_k = p.k / (32 * (32 / BITS));           // 32-word blocks per weight row
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&s.tok_full[i], 1);
       mbar_init(&s.tok_empty[i], 1);
+      mbar_init(&s.wsm_full[i], 1);
+      mbar_init(&s.wsm_empty[i], 128);
+      mbar_init(&s.wtm_full[i], 128);
+      mbar_init(&s.wtm_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s.w_full[i], 128);
-      mbar_init(&s.w_empty[i], 1);
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 128);
     }
-    mbar_init(&s.acc_full, 1);
     s.err = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == MMA_WARP) {
     tmem_alloc(&s.tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
@@ -130,144 +132,219 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_i8_kernel(const __grid_consta
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
-  if (warp == 4) {
-    // ---- TMA producer ----------------------------------------------------------------
+  if (warp == TMA_WARP) {
+    // ---- TMA producer ------------------------------------------------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&tmap);
-      for (int kb = 0; kb < k_blocks; ++kb) {
-        const int st = kb % NS;
-        const uint32_t ph = (kb / NS) & 1;
-        if (!mbar_wait_bounded(&s.tok_empty[st], ph ^ 1, &s.err, 1)) break;
-        mbar_arrive_expect_tx(&s.tok_full[st], STAGE_BYTES);
-        uint8_t *dst = ring + st * STAGE_BYTES;
-        tma_load_2d(dst, &tmap, &s.tok_full[st], kb * KB, (int)row0);
-        tma_load_2d(dst + STAGE_BYTES / 2, &tmap, &s.tok_full[st], kb * KB + 128, (int)row0);
-      }
-    }
-  } else if (warp == 5) {
-    // ---- MMA issuer ------------------------------------------------------------------
-    if (lane == 0) {
+      tma_prefetch_desc(&tok_map);
+      tma_prefetch_desc(&w_map0);
+      tma_prefetch_desc(&w_map1);
+      uint32_t g = 0;
       bool ok = true;
-      for (int kb = 0; kb < k_blocks && ok; ++kb) {
-        const int st = kb % NS;
-        const uint32_t pt = (kb / NS) & 1;
-        const int sw = kb & 1;
-        const uint32_t pw = (kb >> 1) & 1;
-        ok = mbar_wait_bounded(&s.tok_full[st], pt, &s.err, 2) && mbar_wait_bounded(&s.w_full[sw], pw, &s.err, 3);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t b_base = smem_u32(ring + st * STAGE_BYTES);
-#pragma unroll
-        for (int j = 0; j < KB / 32; ++j) {
-          const uint32_t b_addr = b_base + (j >> 2) * (STAGE_BYTES / 2) + (j & 3) * 32;
-          mma_i8_ts(tmem + ACC_COL, tmem + WCOL0 + 64 * sw + 8 * j, smem_desc_sw128(b_addr), IDESC,
-                    (kb | j) != 0);
+      int64_t row0;
+      int rows_valid, n_tile, expert;
+      for (int t = blockIdx.x; ok && tm.get(p, t, row0, rows_valid, n_tile, expert); t += gridDim.x) {
+        const int which = n_tile / p.n_split;
+        const int w_row_tile = expert * p.n_split + (n_tile - which * p.n_split);
+        const CUtensorMap *w_map = which ? &w_map1 : &w_map0;
+        for (int kb = 0; kb < k_stages; ++kb, ++g) {
+          const int st = g % NS;
+          const uint32_t ph = ((g / NS) & 1) ^ 1;
+          if (!(ok = mbar_wait_bounded(&s.tok_empty[st], ph, &s.err, 1) &&
+                     mbar_wait_bounded(&s.wsm_empty[st], ph, &s.err, 1)))
+            break;
+          uint8_t *stage = ring + st * C::STAGE;
+          mbar_arrive_expect_tx(&s.tok_full[st], TOK_BYTES);
+          tma_load_2d(stage, &tok_map, &s.tok_full[st], kb * KS, (int)row0);
+          mbar_arrive_expect_tx(&s.wsm_full[st], C::W_BYTES);
+          if (BITS == 4)
+            tma_load_3d(stage + TOK_BYTES, w_map, &s.wsm_full[st], (kb & 1) * 16, 0,
+                        w_row_tile * blocks_k + (kb >> 1));
+          else
+            tma_load_3d(stage + TOK_BYTES, w_map, &s.wsm_full[st], 0, 0, w_row_tile * blocks_k + kb);
         }
-        mma_commit(&s.tok_empty[st]);
-        mma_commit(&s.w_empty[sw]);
       }
-      mma_commit(&s.acc_full);
+    }
+  } else if (warp == MMA_WARP) {
+    // ---- MMA issuer ----------------------------------------------------------------------
+    if (lane == 0) {
+      uint32_t g = 0;
+      int i = 0;
+      bool ok = true;
+      int64_t row0;
+      int rows_valid, n_tile, expert;
+      for (int t = blockIdx.x; ok && tm.get(p, t, row0, rows_valid, n_tile, expert); t += gridDim.x, ++i) {
+        const int buf = i & 1;
+        if (!(ok = mbar_wait_bounded(&s.acc_empty[buf], ((i >> 1) & 1) ^ 1, &s.err, 7))) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + BN * buf;
+        for (int kb = 0; kb < k_stages; ++kb, ++g) {
+          const int st = g % NS;
+          const uint32_t ph = (g / NS) & 1;
+          if (!(ok = mbar_wait_bounded(&s.tok_full[st], ph, &s.err, 2) &&
+                     mbar_wait_bounded(&s.wtm_full[st], ph, &s.err, 3)))
+            break;
+          tc_fence_after();
+          const uint32_t b_base = smem_u32(ring + st * C::STAGE);
+#pragma unroll
+          for (int j = 0; j < KS / 32; ++j)
+            mma_i8_ts(acc, tmem + WCOL0 + 32 * st + 8 * j, smem_desc_sw128(b_base + 32 * j), IDESC, (kb | j) != 0);
+          mma_commit(&s.tok_empty[st]);
+          mma_commit(&s.wtm_empty[st]);
+        }
+        mma_commit(&s.acc_full[buf]);
+      }
       // Every issued MMA has finished before TMEM is released, on every path.
-      mbar_wait_bounded(&s.acc_full, 0, &s.err, 6);
+      if (i > 0) mbar_wait_bounded(&s.acc_full[(i - 1) & 1], ((i - 1) >> 1) & 1, &s.err, 6);
     }
-  } else {
-    // ---- weight converters (warps 0-3), then epilogue ---------------------------------
-    const int r = warp * 32 + lane;  // weight row within the tile == TMEM lane
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t *wrow = p.w[which] + (w_row_tile * blocks_k) * 4096 + r * words_per_row_block;
+  } else if (warp < CONV_WARPS) {
+    // ---- weight converters (warps 0-7): swizzled smem -> s8 -> TMEM ---------------------
+    const int quarter = warp & 3;
+    const uint32_t parity_group = warp >> 2;  // this group converts stages g with g % 2 == group
+    const int r = quarter * 32 + lane;        // weight row within the tile == TMEM lane
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    uint32_t g = 0;
     bool ok = true;
-    // Wait for weight stage kb % 2 to be free (warp-uniform), returns false on timeout.
-    auto acquire = [&](int kb) -> bool {
-      bool waited = true;
-      if (lane == 0) waited = mbar_wait_bounded(&s.w_empty[kb & 1], ((kb >> 1) & 1) ^ 1, &s.err, 4);
-      waited = __shfl_sync(0xffffffffu, waited, 0) != 0;
-      if (waited) tc_fence_after();
-      return waited;
-    };
-    auto release = [&](int kb) {
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&s.w_full[kb & 1]);
-    };
-    if (p.bits == 4) {
-      // Three register buffers: loads run two K blocks ahead of the TMEM stores.
-      uint32_t b0[32], b1[32], b2[32];
-      auto consume = [&](uint32_t (&b)[32], int kb) -> bool {
-        if (!acquire(kb)) return false;
-        store_block_i4(b, tmem + lane_base + WCOL0 + 64 * (kb & 1));
-        release(kb);
-        return true;
-      };
-      load_words(b0, wrow);
-      if (k_blocks > 1) load_words(b1, wrow + 4096);
-      for (int kb = 0; kb < k_blocks && ok; kb += 3) {
-        if (kb + 2 < k_blocks) load_words(b2, wrow + (int64_t)(kb + 2) * 4096);
-        if (!(ok = consume(b0, kb))) break;
-        if (kb + 1 >= k_blocks) break;
-        if (kb + 3 < k_blocks) load_words(b0, wrow + (int64_t)(kb + 3) * 4096);
-        if (!(ok = consume(b1, kb + 1))) break;
-        if (kb + 2 >= k_blocks) break;
-        if (kb + 4 < k_blocks) load_words(b1, wrow + (int64_t)(kb + 4) * 4096);
-        if (!(ok = consume(b2, kb + 2))) break;
-      }
-    } else {
-      // int8 tiles hold 128 codes per block row: two tiled blocks fill one 256-code stage.
-      for (int kb = 0; kb < k_blocks; ++kb) {
-        uint32_t lo[32], hi[32];
-        load_words(lo, wrow + (int64_t)(2 * kb) * 4096);
-        load_words(hi, wrow + (int64_t)(2 * kb + 1) * 4096);
-        if (!(ok = acquire(kb))) break;
-        tmem_st_x32(tmem + lane_base + WCOL0 + 64 * (kb & 1), lo);
-        tmem_st_x32(tmem + lane_base + WCOL0 + 64 * (kb & 1) + 32, hi);
-        release(kb);
-      }
-    }
-    // ---- epilogue ----------------------------------------------------------------------
-    bool have = ok;
-    if (lane == 0 && have) have = mbar_wait_bounded(&s.acc_full, 0, &s.err, 5);
-    have = __shfl_sync(0xffffffffu, have, 0);
-    if (have) {
-      tc_fence_after();
-      const int n_local = n_tile * BM + r;  // output column
-      const float ws = p.w_scales[which][w_row_tile * BM + r];
-      const int shift = p.bits == 4 ? 8 : 0;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t acc[32];
-        tmem_ld_x32(tmem + lane_base + ACC_COL + c, acc);
-        tmem_ld_wait();
-#pragma unroll 4
-        for (int j = 0; j < 32; ++j) {
-          const int mi = c + j;
-          if (mi >= rows_valid) break;
-          const int64_t pos = row0 + mi;
-          const float a = __int2float_rn((int)acc[j] >> shift);
-          if (GROUPED) {
-            const int64_t route = p.perm[pos];
-            const int64_t sidx = p.scale_mode == 0 ? pos : (p.scale_mode == 1 ? route / p.topk : route);
-            const int64_t orow = p.scatter ? route : pos;
-            const float sc = __fmul_rn(p.a_scales[sidx], ws);
-            p.out[orow * p.ldo + n_local] = f32_to_bf16(__fmul_rn(a, sc));
-          } else {
-            const float y = __fadd_rn(__fmul_rn(__fmul_rn(a, ws), p.a_scales[pos]), 0.0f);
-            if (p.out_f32) {
-              p.out_f32[pos * p.ldo + n_local] = y;
-            } else {
-              const float big = 3.3895313892515355e38f;
-              const float sat = maxnum(minnum(y, big), -big);
-              uint16_t h = f32_to_bf16(fabsf(y) < __int_as_float(0x7f800000) ? sat : y);
-              if (p.residual)
-                h = f32_to_bf16(__fadd_rn(bf16_to_f32(p.residual[pos * p.ldr + n_local]), bf16_to_f32(h)));
-              p.out[pos * p.ldo + n_local] = h;
+    int64_t row0;
+    int rows_valid, n_tile, expert;
+    for (int t = blockIdx.x; ok && tm.get(p, t, row0, rows_valid, n_tile, expert); t += gridDim.x) {
+      for (int kb = 0; kb < k_stages; ++kb, ++g) {
+        if ((g & 1) != parity_group) continue;
+        const int st = g % NS;
+        const uint32_t ph = (g / NS) & 1;
+        bool waited = true;
+        if (lane == 0)
+          waited = mbar_wait_bounded(&s.wsm_full[st], ph, &s.err, 4) &&
+                   mbar_wait_bounded(&s.wtm_empty[st], ph ^ 1, &s.err, 4);
+        waited = __shfl_sync(0xffffffffu, waited, 0) != 0;
+        if (!(ok = waited)) break;
+        tc_fence_after();
+        const uint32_t wbase = smem_u32(ring + st * C::STAGE + TOK_BYTES);
+        uint32_t o[32];
+        if (BITS == 4) {
+          // 64-byte rows, 64-byte swizzle: chunk c of row r sits at chunk c ^ ((r >> 1) & 3)
+          uint32_t w[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 v = lds_v4(wbase + r * 64 + 16 * (c ^ ((r >> 1) & 3)));
+            w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+          }
+          mbar_arrive(&s.wsm_empty[st]);
+#pragma unroll
+          for (int gq = 0; gq < 4; ++gq) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              o[8 * gq + q] = nib_lo16(w[4 * gq + q]);
+              o[8 * gq + 4 + q] = nib_hi16(w[4 * gq + q]);
             }
           }
+        } else {
+          // 128-byte rows, 128-byte swizzle: chunk c of row r sits at chunk c ^ (r & 7)
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 v = lds_v4(wbase + r * 128 + 16 * (c ^ (r & 7)));
+            o[4 * c] = v.x; o[4 * c + 1] = v.y; o[4 * c + 2] = v.z; o[4 * c + 3] = v.w;
+          }
+          mbar_arrive(&s.wsm_empty[st]);
         }
+        tmem_st_x32(tmem + lane_base + WCOL0 + 32 * st, o);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&s.wtm_full[st]);
+      }
+    }
+  } else {
+    // ---- epilogue (warps 10-13) ---------------------------------------------------------
+    // Phase 1: thread r owns output column r; per 32-token chunk it reads its accumulator
+    // lane (tcgen05.ld), takes the token's activation scale from the lane that loaded it
+    // (shuffle), applies the reference epilogue and writes BF16 into the staging tile.
+    // Phase 2: each warp stores 32 token rows, 256 contiguous bytes per row (residual add
+    // and route scatter happen here).
+    const int quarter = warp & 3;        // TMEM lanes this warp may access
+    const int r = quarter * 32 + lane;   // weight row within the tile
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int shift = BITS == 4 ? 8 : 0;
+    const float big = 3.3895313892515355e38f;
+    int i = 0;
+    int64_t row0;
+    int rows_valid, n_tile, expert;
+    for (int t = blockIdx.x; tm.get(p, t, row0, rows_valid, n_tile, expert); t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      bool have = true;
+      if (lane == 0) have = mbar_wait_bounded(&s.acc_full[buf], (i >> 1) & 1, &s.err, 5);
+      have = __shfl_sync(0xffffffffu, have, 0) != 0;
+      // all four epilogue warps agree before any of them reaches a named barrier
+      if (!named_barrier_and(2, 128, have)) break;
+      tc_fence_after();
+      const int which = n_tile / p.n_split;
+      const int64_t w_row = (int64_t)(expert * p.n_split + (n_tile - which * p.n_split)) * BM + r;
+      const float ws = p.w_scales[which][w_row];
+      const int n_local = n_tile * BM + r;  // output column
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t accv[32];
+        tmem_ld_x32(tmem + lane_base + BN * buf + c, accv);
+        // lane j fetches what token c + j needs: its activation scale (and route)
+        const int mj = c + lane;
+        float my_scale = 0.0f;
+        if (mj < rows_valid) {
+          const int64_t pos = row0 + mj;
+          if (GROUPED) {
+            const int64_t route = p.perm[pos];
+            my_scale = p.a_scales[p.scale_mode == 0 ? pos : (p.scale_mode == 1 ? route / p.topk : route)];
+          } else {
+            my_scale = p.a_scales[pos];
+          }
+        }
+        tmem_ld_wait();
+        if (c + 32 >= BN) {
+          tc_fence_before();
+          mbar_arrive(&s.acc_empty[buf]);  // accumulator free for tile i + 2
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float as = __shfl_sync(0xffffffffu, my_scale, j);
+          const float a = __int2float_rn((int)accv[j] >> shift);
+          uint16_t h;
+          if (GROUPED) {
+            h = f32_to_bf16(__fmul_rn(a, __fmul_rn(as, ws)));
+          } else {
+            const float y = __fadd_rn(__fmul_rn(__fmul_rn(a, ws), as), 0.0f);
+            if (p.out_f32) {
+              if (c + j < rows_valid) p.out_f32[(row0 + c + j) * p.ldo + n_local] = y;
+              continue;
+            }
+            const float sat = maxnum(minnum(y, big), -big);
+            h = f32_to_bf16(fabsf(y) < __int_as_float(0x7f800000) ? sat : y);
+          }
+          staging[(c + j) * BM + r] = h;
+        }
+      }
+      if (GROUPED || !p.out_f32) {
+        named_barrier_sync(1, 128);
+        // phase 2: rows quarter*32 .. quarter*32+31, lane covers columns 4*lane .. 4*lane+3
+        for (int m = quarter * 32; m < quarter * 32 + 32 && m < rows_valid; ++m) {
+          const int64_t pos = row0 + m;
+          int64_t orow = pos;
+          if (GROUPED && p.scatter) orow = p.perm[pos];
+          uint2 v = *reinterpret_cast<const uint2 *>(staging + m * BM + 4 * lane);
+          if (!GROUPED && p.residual) {
+            const uint2 rv = *reinterpret_cast<const uint2 *>(p.residual + pos * p.ldr + n_tile * BM + 4 * lane);
+            const uint16_t *hv = reinterpret_cast<const uint16_t *>(&v);
+            const uint16_t *hr = reinterpret_cast<const uint16_t *>(&rv);
+            uint16_t o4[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) o4[q] = f32_to_bf16(__fadd_rn(bf16_to_f32(hr[q]), bf16_to_f32(hv[q])));
+            v = *reinterpret_cast<uint2 *>(o4);
+          }
+          *reinterpret_cast<uint2 *>(p.out + orow * p.ldo + n_tile * BM + 4 * lane) = v;
+        }
+        named_barrier_sync(1, 128);  // staging is reused by the next tile
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -292,18 +369,47 @@ EncodeTiledFn encode_fn() {
 
 }  // namespace
 
+// Weight tiles viewed as a 3D tensor: x = 32 words of one block row, y = 128 rows,
+// z = 128x32-word blocks in (row block, k block) order; one box = the K=128 slice of a
+// row block (16 words for int4, 32 for int8), swizzled to match the converter reads.
+static bool weight_map(EncodeTiledFn enc, CUtensorMap *m, const uint32_t *w, int64_t rows, int k, int bits) {
+  const int64_t blocks = rows / 128 * (k / (32 * (32 / bits)));
+  cuuint64_t dims[3] = {32, 128, (cuuint64_t)blocks};
+  cuuint64_t strides[2] = {128, 16384};
+  cuuint32_t box[3] = {(cuuint32_t)(bits == 4 ? 16 : 32), 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint32_t *>(w), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, bits == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool G, int B>
+static void launch_variant(dim3 grid, const CUtensorMap &t, const CUtensorMap &w0, const CUtensorMap &w1,
+                           const GemmParams &p, cudaStream_t stream) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemm_i8_kernel<G, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<B>::SMEM);
+    attr = true;
+  }
+  gemm_i8_kernel<G, B><<<grid, THREADS, Cfg<B>::SMEM, stream>>>(t, w0, w1, p);
+}
+
 int launch_gemm(const GemmParams &p, cudaStream_t stream) {
-  if (p.n % BM || p.k % KB || p.k <= 0 || p.n <= 0) return CLEFQ_ERR_SHAPE;
+  if (p.n % BM || p.k % 256 || p.k <= 0 || p.n <= 0) return CLEFQ_ERR_SHAPE;
   if (!(p.bits == 4 || p.bits == 8)) return CLEFQ_ERR_SHAPE;
   if ((uintptr_t)p.a_op % 16 || p.a_ld % 16 || p.a_ld < p.k) return CLEFQ_ERR_ALIGN;
-  if ((uintptr_t)p.w[0] % 16 || (p.n / BM > p.n_split && (uintptr_t)p.w[1] % 16)) return CLEFQ_ERR_ALIGN;
+  const bool two = p.n / BM > p.n_split;
   if (p.n_split <= 0 || (p.n / BM) % p.n_split || p.n / BM > 2 * p.n_split) return CLEFQ_ERR_SHAPE;
+  if ((uintptr_t)p.w[0] % 16 || (two && (uintptr_t)p.w[1] % 16)) return CLEFQ_ERR_ALIGN;
+  // the epilogue stores 8-byte groups of four BF16 columns
+  if (p.out && ((uintptr_t)p.out % 8 || p.ldo % 4)) return CLEFQ_ERR_ALIGN;
+  if (p.residual && ((uintptr_t)p.residual % 8 || p.ldr % 4)) return CLEFQ_ERR_ALIGN;
   const int64_t tiles_m = p.grouped ? p.max_tiles : (p.m + BN - 1) / BN;
   if (tiles_m == 0 || p.a_rows == 0) return 0;
-  if (tiles_m > 65535) return CLEFQ_ERR_SHAPE;
+  if (tiles_m * (p.n / BM) > 0x7fffffff) return CLEFQ_ERR_SHAPE;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return CLEFQ_ERR_CUDA;
-  CUtensorMap tmap;
+  CUtensorMap tmap, wmap0, wmap1;
   cuuint64_t dims[2] = {(cuuint64_t)p.k, (cuuint64_t)p.a_rows};
   cuuint64_t strides[1] = {(cuuint64_t)p.a_ld};
   cuuint32_t box[2] = {128, (cuuint32_t)BN};
@@ -312,20 +418,25 @@ int launch_gemm(const GemmParams &p, cudaStream_t stream) {
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (rc != CUDA_SUCCESS) return CLEFQ_ERR_CUDA;
-  static bool attr_set[2] = {false, false};
-  dim3 grid(p.n / BM, (unsigned)tiles_m);
-  if (p.grouped) {
-    if (!attr_set[1]) {
-      cudaFuncSetAttribute(gemm_i8_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-      attr_set[1] = true;
-    }
-    gemm_i8_kernel<true><<<grid, THREADS, SMEM_BYTES, stream>>>(tmap, p);
+  const int64_t experts = p.grouped ? p.experts : 1;
+  const int64_t wrows = experts * p.n_split * (int64_t)BM;
+  if (!weight_map(enc, &wmap0, p.w[0], wrows, p.k, p.bits)) return CLEFQ_ERR_CUDA;
+  if (two) {
+    if (!weight_map(enc, &wmap1, p.w[1], wrows, p.k, p.bits)) return CLEFQ_ERR_CUDA;
   } else {
-    if (!attr_set[0]) {
-      cudaFuncSetAttribute(gemm_i8_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-      attr_set[0] = true;
-    }
-    gemm_i8_kernel<false><<<grid, THREADS, SMEM_BYTES, stream>>>(tmap, p);
+    wmap1 = wmap0;
+  }
+  // Persistent grid: one CTA per SM (grouped launches do not know their tile count on
+  // the host; surplus CTAs exit at once).
+  const int64_t total = tiles_m * (p.n / BM);
+  const int sms = device_sms();
+  dim3 grid((unsigned)(total < sms ? total : sms));
+  if (p.grouped) {
+    if (p.bits == 4) launch_variant<true, 4>(grid, tmap, wmap0, wmap1, p, stream);
+    else launch_variant<true, 8>(grid, tmap, wmap0, wmap1, p, stream);
+  } else {
+    if (p.bits == 4) launch_variant<false, 4>(grid, tmap, wmap0, wmap1, p, stream);
+    else launch_variant<false, 8>(grid, tmap, wmap0, wmap1, p, stream);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
 }

@@ -36,3 +36,13 @@ def permuted_operand(codes_words: np.ndarray, width: int) -> np.ndarray:
     lo = lo.reshape(rows, -1, 4)
     hi = hi.reshape(rows, -1, 4)
     return np.concatenate([lo, hi], axis=2).reshape(rows, -1).view(np.int8).reshape(rows, width)
+
+
+def bf16_equal_nan(a, b) -> bool:
+    """Bit equality of BF16 arrays where any two NaNs count as equal (NaN payloads are not
+    part of the contract: the GPU produces canonical NaNs, the host propagates payloads)."""
+    from oracle import oracle as o
+    a = np.asarray(a, dtype=np.uint16)
+    b = np.asarray(b, dtype=np.uint16)
+    na, nb = np.isnan(o.bf16_to_f32(a)), np.isnan(o.bf16_to_f32(b))
+    return np.array_equal(na, nb) and np.array_equal(a[~na], b[~nb])

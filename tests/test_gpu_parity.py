@@ -10,7 +10,8 @@ import pytest
 import torch
 
 from oracle import oracle as o
-from tests.gpu_util import bf16_normal, from_dev_bf16, permuted_operand, same_bits_f32, to_dev, to_dev_bf16
+from tests.gpu_util import (bf16_equal_nan, bf16_normal, from_dev_bf16, permuted_operand, same_bits_f32, to_dev,
+                            to_dev_bf16)
 
 pytestmark = pytest.mark.gpu
 
@@ -103,7 +104,7 @@ def test_fused_swiglu_packing(cq, rows, width, bits):
     storage, _, _, _ = o.prepare(g, bits, stride, o.SWIGLU, u)
     assert np.array_equal(fused.storage.cpu().numpy().view(np.uint32), storage)
     act = cq.swiglu(to_dev_bf16(g), to_dev_bf16(u))
-    assert np.array_equal(from_dev_bf16(act), o.swiglu(g, u))
+    assert bf16_equal_nan(from_dev_bf16(act), o.swiglu(g, u))
     sep = cq.prepare(act, bits, stride)
     assert torch.equal(sep.storage, fused.storage)
 
