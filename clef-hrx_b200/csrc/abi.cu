@@ -10,12 +10,12 @@
 namespace cq {
 int launch_route(const void *logits, int is_f32, int64_t tokens, int experts, int topk, float *routes,
                  cudaStream_t stream);
-int launch_group(const float *routes, int64_t tokens, int topk, int experts, int *counts, int *offsets,
+int launch_group(const float *routes, int64_t tokens, int topk, int experts, int tile_rows, int *counts, int *offsets,
                  int *tile_list, int *perm, float *groups, float *order, float *tasks, cudaStream_t stream,
                  int num_sms);
 int launch_tasks(const float *groups, int64_t tokens, int experts, float *tasks, cudaStream_t stream);
-int launch_groups_to_sorted(const float *groups, int64_t tokens, int topk, int experts, int *offsets, int *perm,
-                            int *tile_list, cudaStream_t stream);
+int launch_groups_to_sorted(const float *groups, int64_t tokens, int topk, int experts, int tile_rows, int *offsets,
+                            int *perm, int *tile_list, cudaStream_t stream);
 int launch_gather(const uint8_t *src, int64_t src_ld, const int *perm, int div, int64_t rows, int64_t row_bytes,
                   uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms);
 int launch_gather_unpack_i4(const uint32_t *a, int64_t a_ld, const int *perm, int div, int64_t rows, int k,
@@ -315,7 +315,7 @@ int clefq_group_routes(void *stream, const float *routes, int64_t tokens, int to
   Arena a = group_tables(Arena{static_cast<uint8_t *>(workspace), workspace_bytes}, tokens, topk, experts, &counts,
                          &offsets, &tiles, &perm);
   if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "group workspace too small");
-  int rc = launch_group(routes, tokens, topk, experts, counts, offsets, tiles, perm, groups, order, nullptr,
+  int rc = launch_group(routes, tokens, topk, experts, 128, counts, offsets, tiles, perm, groups, order, nullptr,
                         static_cast<cudaStream_t>(stream), device_sms());
   return rc ? cuda_err("group launch") : 0;
 }
@@ -358,7 +358,8 @@ int clefq_expert(void *stream, const void *a_codes, int64_t a_ld_words, const fl
                           &offsets, &tiles, &perm, &op);
   if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "expert workspace too small");
   const int64_t routes = tokens * topk;
-  int rc = launch_groups_to_sorted(groups, tokens, topk, experts, offsets, perm, tiles, s);
+  const int tile_rows = gemm_tile_rows((int)n, (int)(n / 128));
+  int rc = launch_groups_to_sorted(groups, tokens, topk, experts, tile_rows, offsets, perm, tiles, s);
   if (!rc)
     rc = launch_gather_unpack_i4(static_cast<const uint32_t *>(a_codes), a_ld_words, perm, input_routed ? 1 : topk,
                                  routes, (int)k, op, k, s, device_sms());
@@ -382,8 +383,9 @@ int clefq_expert(void *stream, const void *a_codes, int64_t a_ld_words, const fl
   p.tile_list = tiles;
   p.expert_offsets = offsets;
   p.perm = perm;
-  p.max_tiles = (int)((routes + 127) / 128 + experts);
+  p.max_tiles = (int)((routes + tile_rows - 1) / tile_rows + experts);
   p.experts = experts;
+  p.tile_rows = tile_rows;
   p.topk = topk;
   p.scale_mode = input_routed ? 2 : 1;
   p.scatter = 1;
@@ -499,10 +501,15 @@ int clefq_moe(void *stream, const void *x, const void *logits, int logits_dtype,
   float *routes = routes_out ? routes_out : t.routes;
   const int64_t nroutes = tokens * topk;
   const int sms = device_sms();
+  // One tile list serves both expert GEMMs: both must run the same kernel family.
+  const int tile_rows = gemm_tile_rows((int)(2 * inter), (int)(inter / 128));
+  if (gemm_tile_rows((int)hidden, (int)(hidden / 128)) != tile_rows) {
+    return set_err(CLEFQ_ERR_SHAPE, "hidden and intermediate must both be multiples of 256, or neither");
+  }
   int rc = launch_route(logits, logits_dtype == CLEFQ_F32, tokens, experts, topk, routes, s);
   if (!rc)
-    rc = launch_group(routes, tokens, topk, experts, t.counts, t.offsets, t.tiles, t.perm, nullptr, t.order, nullptr,
-                      s, sms);
+    rc = launch_group(routes, tokens, topk, experts, tile_rows, t.counts, t.offsets, t.tiles, t.perm, nullptr, t.order,
+                      nullptr, s, sms);
   if (rc) return cuda_err("routing launch");
   const int64_t sh = stride_for(hidden);
   rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, tokens, hidden, sh, t.xq, t.x8, hidden, nullptr, 0);
@@ -530,8 +537,9 @@ int clefq_moe(void *stream, const void *x, const void *logits, int logits_dtype,
   p.tile_list = t.tiles;
   p.expert_offsets = t.offsets;
   p.perm = t.perm;
-  p.max_tiles = (int)((nroutes + 127) / 128 + experts);
+  p.max_tiles = (int)((nroutes + tile_rows - 1) / tile_rows + experts);
   p.experts = experts;
+  p.tile_rows = tile_rows;
   p.topk = topk;
   p.scale_mode = 1;  // activation scale of the token
   p.scatter = 0;     // rows stay in expert-sorted order

@@ -57,12 +57,16 @@ struct GemmParams {
   const int *perm;          // sorted position -> route id
   int max_tiles;
   int experts;              // experts whose weights are stacked in w[] (grouped)
+  int tile_rows;            // token rows per tile-list entry (gemm_tile_rows)
   int topk;
   int scale_mode;           // a_scales index: 0 -> p, 1 -> perm[p] / topk, 2 -> perm[p]
   int scatter;              // output row: 1 -> perm[p], 0 -> p
   int *err;                 // device status word
 };
 int launch_gemm(const GemmParams &p, cudaStream_t stream);
+// Token rows per tile of the kernel launch_gemm picks for this output shape (grouped
+// callers build their tile lists with it).
+int gemm_tile_rows(int n, int n_split);
 
 int device_sms();
 int *device_status_word();  // per-device zero-initialised status word used by bounded waits

@@ -256,4 +256,75 @@ CQ_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "
 
 CQ_DEV uint4 ldg_nc_v4(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 
+// --- clusters and 2-SM (cta_group::2) forms --------------------------------------------
+CQ_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+CQ_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of the same shared variable in CTA `rank` of this cluster.
+CQ_DEV uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+// Arrive on a barrier of another CTA of the cluster (default .release.cta semantics; a
+// .cluster-scope release here costs ~1.5k cycles per call and serialised the pair
+// pipeline).  Ordering of tensor-memory writes is given by tcgen05.wait::st and
+// tcgen05.fence::before_thread_sync ahead of the arrive.
+CQ_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Asynchronous cross-CTA signal: stores 4 bytes into shared word `word` of another CTA
+// and counts them as completed transaction bytes on that CTA's barrier `bar` (both are
+// cluster addresses).  The issuing thread does not wait for the round trip, unlike a
+// remote mbarrier.arrive.
+CQ_DEV void st_async_signal(uint32_t word, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.u32 [%0], %1, [%2];" ::"r"(word), "r"(1u),
+               "r"(bar)
+               : "memory");
+}
+CQ_DEV void mbar_arrive_expect_tx_u32(uint32_t bar_addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_addr), "r"(bytes) : "memory");
+}
+// 2D tiled TMA load into this CTA's shared memory whose completion is counted on the
+// barrier at cluster address `bar` (the pair leader's), as the 2-SM MMA requires.
+CQ_DEV void tma_load_2d_cg2(void *dst, const void *desc, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(desc), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+CQ_DEV void tmem_alloc2(uint32_t *slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+               "r"(ncols)
+               : "memory");
+}
+CQ_DEV void tmem_relinquish2() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory"); }
+CQ_DEV void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A[tmem] x B[smem desc] across the CTA pair (M = 256 rows, 128 per CTA;
+// B's N rows split in halves between the two CTAs' shared memory at the same offset).
+CQ_DEV void mma_i8_ts2(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the barrier at this shared offset in every CTA of `mask` when the pair's
+// previously issued MMAs complete.
+CQ_DEV void mma_commit2_mc(uint64_t *bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
 }  // namespace cq

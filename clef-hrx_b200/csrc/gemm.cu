@@ -146,7 +146,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int which = n_tile / p.n_split;
         const int w_row_tile = expert * p.n_split + (n_tile - which * p.n_split);
         const CUtensorMap *w_map = which ? &w_map1 : &w_map0;
-        for (int kb = 0; kb < k_stages; ++kb, ++g) {
+        // staggered K start per tile (exact integer sums; spreads concurrent L2 reads)
+        const int k_off = (int)((7u * (uint32_t)t) % (uint32_t)k_stages);
+        for (int kk = 0; kk < k_stages; ++kk, ++g) {
+          const int kb = kk + k_off < k_stages ? kk + k_off : kk + k_off - k_stages;
           const int st = g % NS;
           const uint32_t ph = ((g / NS) & 1) ^ 1;
           if (!(ok = mbar_wait_bounded(&s.tok_empty[st], ph, &s.err, 1) &&
@@ -351,6 +354,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0 && s.err) atomicCAS(p.err, 0, s.err);
 }
 
+#include "gemm2sm.cuh"
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -394,6 +399,40 @@ static void launch_variant(dim3 grid, const CUtensorMap &t, const CUtensorMap &w
   gemm_i8_kernel<G, B><<<grid, THREADS, Cfg<B>::SMEM, stream>>>(t, w0, w1, p);
 }
 
+// Launch the pair kernel on as many co-resident clusters of 2 as the device holds.
+template <bool G, int B>
+static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, const CUtensorMap &w0,
+                                      const CUtensorMap &w1, const GemmParams &p, cudaStream_t stream) {
+  using namespace two_sm;
+  static int max_clusters = 0;
+  auto kern = gemm_i8_2sm_kernel<G, B>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(THREADS2);
+  cfg.dynamicSmemBytes = Cfg2<B>::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!max_clusters) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<B>::SMEM);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(2 * 74);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = device_sms() / 2;
+    max_clusters = n;
+  }
+  const int64_t clusters = pair_tiles < max_clusters ? pair_tiles : max_clusters;
+  cfg.gridDim = dim3((unsigned)(2 * clusters));
+  return cudaLaunchKernelEx(&cfg, kern, t, w0, w1, p);
+}
+
+bool gemm_uses_pairs(const GemmParams &p) { return p.n_split % 2 == 0 && p.n % 256 == 0; }
+int gemm_tile_rows(int n, int n_split) { return (n_split % 2 == 0 && n % 256 == 0) ? two_sm::BN2 : BN; }
+
 int launch_gemm(const GemmParams &p, cudaStream_t stream) {
   if (p.n % BM || p.k % 256 || p.k <= 0 || p.n <= 0) return CLEFQ_ERR_SHAPE;
   if (!(p.bits == 4 || p.bits == 8)) return CLEFQ_ERR_SHAPE;
@@ -404,7 +443,10 @@ int launch_gemm(const GemmParams &p, cudaStream_t stream) {
   // the epilogue stores 8-byte groups of four BF16 columns
   if (p.out && ((uintptr_t)p.out % 8 || p.ldo % 4)) return CLEFQ_ERR_ALIGN;
   if (p.residual && ((uintptr_t)p.residual % 8 || p.ldr % 4)) return CLEFQ_ERR_ALIGN;
-  const int64_t tiles_m = p.grouped ? p.max_tiles : (p.m + BN - 1) / BN;
+  const bool pairs = gemm_uses_pairs(p);
+  const int tile_rows = pairs ? two_sm::BN2 : BN;
+  if (p.grouped && p.tile_rows != tile_rows) return CLEFQ_ERR_SHAPE;  // tile list built for the other kernel
+  const int64_t tiles_m = p.grouped ? p.max_tiles : (p.m + tile_rows - 1) / tile_rows;
   if (tiles_m == 0 || p.a_rows == 0) return 0;
   if (tiles_m * (p.n / BM) > 0x7fffffff) return CLEFQ_ERR_SHAPE;
   EncodeTiledFn enc = encode_fn();
@@ -412,7 +454,7 @@ int launch_gemm(const GemmParams &p, cudaStream_t stream) {
   CUtensorMap tmap, wmap0, wmap1;
   cuuint64_t dims[2] = {(cuuint64_t)p.k, (cuuint64_t)p.a_rows};
   cuuint64_t strides[1] = {(cuuint64_t)p.a_ld};
-  cuuint32_t box[2] = {128, (cuuint32_t)BN};
+  cuuint32_t box[2] = {128, (cuuint32_t)(pairs ? two_sm::HALF : BN)};
   cuuint32_t estr[2] = {1, 1};
   CUresult rc = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(p.a_op), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -425,6 +467,17 @@ int launch_gemm(const GemmParams &p, cudaStream_t stream) {
     if (!weight_map(enc, &wmap1, p.w[1], wrows, p.k, p.bits)) return CLEFQ_ERR_CUDA;
   } else {
     wmap1 = wmap0;
+  }
+  if (pairs) {
+    const int64_t pair_tiles = tiles_m * (p.n / two_sm::BMP);
+    cudaError_t e;
+    if (p.grouped)
+      e = p.bits == 4 ? launch_variant_2sm<true, 4>(pair_tiles, tmap, wmap0, wmap1, p, stream)
+                      : launch_variant_2sm<true, 8>(pair_tiles, tmap, wmap0, wmap1, p, stream);
+    else
+      e = p.bits == 4 ? launch_variant_2sm<false, 4>(pair_tiles, tmap, wmap0, wmap1, p, stream)
+                      : launch_variant_2sm<false, 8>(pair_tiles, tmap, wmap0, wmap1, p, stream);
+    return e == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
   }
   // Persistent grid: one CTA per SM (grouped launches do not know their tile count on
   // the host; surplus CTAs exit at once).

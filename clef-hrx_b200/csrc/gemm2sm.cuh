@@ -1,0 +1,360 @@
+// clefq: the 2-SM (cta_group::2) INT4/INT8 GEMM used when every weight matrix has a
+// multiple of 256 output rows.  Included by gemm.cu (shares its helpers and epilogue
+// arithmetic).
+//
+// A CTA pair (cluster of 2) computes one 256-weight-row x 192-token tile:
+//   * each CTA converts its own 128 weight rows into its TMEM (the MMA's A operand),
+//   * each CTA TMA-loads its own 96 token rows (the B operand is split along N between the
+//     pair's shared memory); the loads use the .cta_group::2 form so that both halves count
+//     on the leader's barrier -- plain loads, no multicast,
+//   * the leader issues tcgen05.mma.cta_group::2 (M=256, N=192, K=32) and multicasts each
+//     completion (tcgen05.commit) to both CTAs,
+//   * both CTAs drain their 128-row slice of the accumulator; accumulators are double
+//     buffered (2 x 192 TMEM columns) so a tile's epilogue overlaps the next mainloop.
+// Per SM this moves 20 KB of operands per 384 MMA cycles (~53 B/clk), under the ~67 B/clk
+// the L2 delivers to one SM, where the 128 x 128 one-CTA tile needs ~96 B/clk.
+#pragma once
+
+namespace two_sm {
+
+constexpr int BMP = 256;                       // weight rows per pair tile (128 per CTA)
+constexpr int BN2 = 192;                       // tokens per pair tile (96 per CTA)
+constexpr int HALF = 96;                       // token rows held by one CTA
+constexpr int KS2 = 128;                       // codes per stage
+constexpr int TOK_B = HALF * KS2;              // 12 KiB
+constexpr int NSW = 4;                         // TMEM weight stages
+constexpr int ACC_COLS = 192;
+constexpr int WCOL = 2 * ACC_COLS;             // 384: weight stages after both accumulators
+constexpr int TMEM2_COLS = 512;
+constexpr int THREADS2 = 320;                  // 4 converter, 1 TMA, 1 MMA, 4 epilogue warps
+constexpr int TMA_W = 4, MMA_W = 5;
+constexpr uint32_t IDESC2 = idesc_i8(256, BN2);
+constexpr int STAGING2 = BN2 * 128 * 2;        // 48 KiB BF16 [token][column]
+
+template <int BITS>
+struct Cfg2 {
+  static constexpr int NS = BITS == 4 ? 8 : 6;
+  static constexpr int W_BYTES = 128 * KS2 * BITS / 8;
+  static constexpr int STAGE = TOK_B + W_BYTES;
+  static constexpr int SMEM = NS * STAGE + STAGING2 + 1024 + 1024;
+};
+
+template <int NS>
+struct Smem2 {
+  uint64_t tok_full[NS], tok_empty[NS], wsm_full[NS], wsm_empty[NS];
+  uint64_t wtm_full[NSW], wtm_empty[NSW], acc_full[2], acc_empty[2];
+  uint32_t sink[8];  // targets of the follower's asynchronous 4-byte signals
+  uint32_t tmem_base;
+  int err;
+};
+
+struct TileMap2 {
+  int n_pairs, total;
+  CQ_DEV bool get(const GemmParams &p, int t, int64_t &row0, int &rows_valid, int &np, int &expert) const {
+    if (t >= total) return false;
+    const int mt = t / n_pairs;
+    np = t - mt * n_pairs;
+    if (p.grouped) {
+      expert = p.tile_list[1 + 2 * mt];
+      row0 = p.tile_list[2 + 2 * mt];
+      const int64_t end = p.expert_offsets[expert + 1];
+      rows_valid = (int)(end - row0 < BN2 ? end - row0 : BN2);
+    } else {
+      expert = 0;
+      row0 = (int64_t)mt * BN2;
+      rows_valid = (int)(p.m - row0 < BN2 ? p.m - row0 : BN2);
+    }
+    return true;
+  }
+};
+
+template <bool GROUPED, int BITS>
+__global__ void __launch_bounds__(THREADS2, 1)
+    gemm_i8_2sm_kernel(const __grid_constant__ CUtensorMap tok_map, const __grid_constant__ CUtensorMap w_map0,
+                       const __grid_constant__ CUtensorMap w_map1, GemmParams p) {
+  using C = Cfg2<BITS>;
+  constexpr int NS = C::NS;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *ring = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint16_t *staging = reinterpret_cast<uint16_t *>(ring + NS * C::STAGE);
+  Smem2<NS> &s = *reinterpret_cast<Smem2<NS> *>(ring + NS * C::STAGE + STAGING2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+  TileMap2 tm;
+  tm.n_pairs = p.n / BMP;
+  tm.total = (GROUPED ? p.tile_list[0] : (int)((p.m + BN2 - 1) / BN2)) * tm.n_pairs;
+  if (cluster >= tm.total) return;  // uniform across the pair
+  const int k_stages = p.k / KS2;
+  const int blocks_k = p.k / (32 * (32 / BITS));
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&s.tok_full[i], 1);
+      mbar_init(&s.tok_empty[i], 1);
+      mbar_init(&s.wsm_full[i], 1);
+      mbar_init(&s.wsm_empty[i], 128);
+    }
+    // wtm_full / acc_empty (used on the leader): 4 local warp arrivals, one of which
+    // also expects the follower's 4 x 4 signal bytes (st.async complete_tx).
+    for (int i = 0; i < NSW; ++i) {
+      mbar_init(&s.wtm_full[i], 4);
+      mbar_init(&s.wtm_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 4);
+    }
+    s.err = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_W) {
+    tmem_alloc2(&s.tmem_base, TMEM2_COLS);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  // Output/weight tile of this CTA for pair tile np: 128-row tile 2*np + rank.
+  auto weight_tile = [&](int np, int expert, int &which, int &w_row_tile) {
+    const int nt = 2 * np + (int)rank;
+    which = nt / p.n_split;
+    w_row_tile = expert * p.n_split + (nt - which * p.n_split);
+  };
+
+  if (warp == TMA_W) {
+    // ---- TMA producer (both CTAs) -------------------------------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tok_map);
+      tma_prefetch_desc(&w_map0);
+      tma_prefetch_desc(&w_map1);
+      uint32_t g = 0;
+      bool ok = true;
+      int64_t row0;
+      int rows_valid, np, expert;
+      for (int t = cluster; ok && tm.get(p, t, row0, rows_valid, np, expert); t += nclusters) {
+        int which, w_row_tile;
+        weight_tile(np, expert, which, w_row_tile);
+        const CUtensorMap *w_map = which ? &w_map1 : &w_map0;
+        // Integer accumulation is exact in any order, so each pair tile starts its K sweep
+        // at its own offset: pairs sharing a token tile then read different K slices at the
+        // same moment instead of hammering the same L2 lines.
+        const int k_off = (int)((7u * (uint32_t)t) % (uint32_t)k_stages);
+        for (int kk = 0; kk < k_stages; ++kk, ++g) {
+          const int kb = kk + k_off < k_stages ? kk + k_off : kk + k_off - k_stages;
+          const int st = g % NS;
+          const uint32_t ph = ((g / NS) & 1) ^ 1;
+          if (!(ok = mbar_wait_bounded(&s.tok_empty[st], ph, &s.err, 1) &&
+                     mbar_wait_bounded(&s.wsm_empty[st], ph, &s.err, 1)))
+            break;
+          uint8_t *stage = ring + st * C::STAGE;
+          if (rank == 0) mbar_arrive_expect_tx(&s.tok_full[st], 2 * TOK_B);
+          tma_load_2d_cg2(stage, &tok_map, mapa_shared(smem_u32(&s.tok_full[st]), 0), kb * KS2,
+                          (int)(row0 + HALF * rank));
+          mbar_arrive_expect_tx(&s.wsm_full[st], C::W_BYTES);
+          if (BITS == 4)
+            tma_load_3d(stage + TOK_B, w_map, &s.wsm_full[st], (kb & 1) * 16, 0, w_row_tile * blocks_k + (kb >> 1));
+          else
+            tma_load_3d(stage + TOK_B, w_map, &s.wsm_full[st], 0, 0, w_row_tile * blocks_k + kb);
+        }
+      }
+    }
+  } else if (warp == MMA_W) {
+    // ---- MMA issuer (pair leader only) ---------------------------------------------------
+    if (lane == 0 && rank == 0) {
+      uint32_t g = 0;
+      int i = 0;
+      bool ok = true;
+      int64_t row0;
+      int rows_valid, np, expert;
+      for (int t = cluster; ok && tm.get(p, t, row0, rows_valid, np, expert); t += nclusters, ++i) {
+        const int buf = i & 1;
+        if (!(ok = mbar_wait_bounded(&s.acc_empty[buf], ((i >> 1) & 1) ^ 1, &s.err, 7))) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + ACC_COLS * buf;
+        for (int kb = 0; kb < k_stages; ++kb, ++g) {
+          const int st = g % NS;
+          const int sw = g % NSW;
+          if (!(ok = mbar_wait_bounded(&s.tok_full[st], (g / NS) & 1, &s.err, 2) &&
+                     mbar_wait_bounded(&s.wtm_full[sw], (g / NSW) & 1, &s.err, 3)))
+            break;
+          tc_fence_after();
+          const uint32_t b_base = smem_u32(ring + st * C::STAGE);
+#pragma unroll
+          for (int j = 0; j < KS2 / 32; ++j)
+            mma_i8_ts2(acc, tmem + WCOL + 32 * sw + 8 * j, smem_desc_sw128(b_base + 32 * j), IDESC2, (kb | j) != 0);
+          mma_commit2_mc(&s.tok_empty[st], 3);
+          mma_commit2_mc(&s.wtm_empty[sw], 3);
+        }
+        mma_commit2_mc(&s.acc_full[buf], 3);
+      }
+      if (i > 0) mbar_wait_bounded(&s.acc_full[(i - 1) & 1], ((i - 1) >> 1) & 1, &s.err, 6);
+    }
+  } else if (warp < 4) {
+    // ---- weight converters (both CTAs) -> own TMEM; stage-ready counted on the leader ----
+    const int r = warp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lead_wtm_full = mapa_shared(smem_u32(&s.wtm_full[0]), 0);
+    const uint32_t lead_sink = mapa_shared(smem_u32(&s.sink[warp]), 0);
+    uint32_t g = 0;
+    bool ok = true;
+    int64_t row0;
+    int rows_valid, np, expert;
+    for (int t = cluster; ok && tm.get(p, t, row0, rows_valid, np, expert); t += nclusters) {
+      for (int kb = 0; kb < k_stages; ++kb, ++g) {
+        const int st = g % NS;
+        const int sw = g % NSW;
+        bool waited = true;
+        if (lane == 0)
+          waited = mbar_wait_bounded(&s.wsm_full[st], (g / NS) & 1, &s.err, 4) &&
+                   mbar_wait_bounded(&s.wtm_empty[sw], ((g / NSW) & 1) ^ 1, &s.err, 4);
+        waited = __shfl_sync(0xffffffffu, waited, 0) != 0;
+        if (!(ok = waited)) break;
+        tc_fence_after();
+        const uint32_t wbase = smem_u32(ring + st * C::STAGE + TOK_B);
+        uint32_t o[32];
+        if (BITS == 4) {
+          uint32_t w[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 v = lds_v4(wbase + r * 64 + 16 * (c ^ ((r >> 1) & 3)));
+            w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+          }
+          mbar_arrive(&s.wsm_empty[st]);
+#pragma unroll
+          for (int gq = 0; gq < 4; ++gq) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              o[8 * gq + q] = nib_lo16(w[4 * gq + q]);
+              o[8 * gq + 4 + q] = nib_hi16(w[4 * gq + q]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 v = lds_v4(wbase + r * 128 + 16 * (c ^ (r & 7)));
+            o[4 * c] = v.x; o[4 * c + 1] = v.y; o[4 * c + 2] = v.z; o[4 * c + 3] = v.w;
+          }
+          mbar_arrive(&s.wsm_empty[st]);
+        }
+        tmem_st_x32(tmem + lane_base + WCOL + 32 * sw, o);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0) {
+            if (warp == 0) mbar_arrive_expect_tx(&s.wtm_full[sw], 16);
+            else mbar_arrive(&s.wtm_full[sw]);
+          } else {
+            st_async_signal(lead_sink, lead_wtm_full + 8 * sw);
+          }
+        }
+      }
+    }
+  } else {
+    // ---- epilogue (warps 6-9, both CTAs): this CTA's 128 weight rows x 192 tokens -------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t lead_acc_empty = mapa_shared(smem_u32(&s.acc_empty[0]), 0);
+    const uint32_t lead_sink = mapa_shared(smem_u32(&s.sink[4 + quarter]), 0);
+    const int shift = BITS == 4 ? 8 : 0;
+    const float big = 3.3895313892515355e38f;
+    int i = 0;
+    int64_t row0;
+    int rows_valid, np, expert;
+    for (int t = cluster; tm.get(p, t, row0, rows_valid, np, expert); t += nclusters, ++i) {
+      const int buf = i & 1;
+      bool have = true;
+      if (lane == 0) have = mbar_wait_bounded(&s.acc_full[buf], (i >> 1) & 1, &s.err, 5);
+      have = __shfl_sync(0xffffffffu, have, 0) != 0;
+      if (!named_barrier_and(2, 128, have)) break;
+      tc_fence_after();
+      int which, w_row_tile;
+      weight_tile(np, expert, which, w_row_tile);
+      const float ws = p.w_scales[which][(int64_t)w_row_tile * 128 + r];
+      const int col0 = (2 * np + (int)rank) * 128;  // first output column of this CTA
+#pragma unroll 1
+      for (int c = 0; c < BN2; c += 32) {
+        uint32_t accv[32];
+        tmem_ld_x32(tmem + lane_base + ACC_COLS * buf + c, accv);
+        const int mj = c + lane;
+        float my_scale = 0.0f;
+        if (mj < rows_valid) {
+          const int64_t pos = row0 + mj;
+          if (GROUPED) {
+            const int64_t route = p.perm[pos];
+            my_scale = p.a_scales[p.scale_mode == 0 ? pos : (p.scale_mode == 1 ? route / p.topk : route)];
+          } else {
+            my_scale = p.a_scales[pos];
+          }
+        }
+        tmem_ld_wait();
+        if (c + 32 >= BN2) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (rank == 0) {
+              if (quarter == 0) mbar_arrive_expect_tx(&s.acc_empty[buf], 16);
+              else mbar_arrive(&s.acc_empty[buf]);
+            } else {
+              st_async_signal(lead_sink, lead_acc_empty + 8 * buf);
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float as = __shfl_sync(0xffffffffu, my_scale, j);
+          const float a = __int2float_rn((int)accv[j] >> shift);
+          uint16_t h;
+          if (GROUPED) {
+            h = f32_to_bf16(__fmul_rn(a, __fmul_rn(as, ws)));
+          } else {
+            const float y = __fadd_rn(__fmul_rn(__fmul_rn(a, ws), as), 0.0f);
+            if (p.out_f32) {
+              if (c + j < rows_valid) p.out_f32[(row0 + c + j) * p.ldo + col0 + r] = y;
+              continue;
+            }
+            const float sat = maxnum(minnum(y, big), -big);
+            h = f32_to_bf16(fabsf(y) < __int_as_float(0x7f800000) ? sat : y);
+          }
+          staging[(c + j) * 128 + r] = h;
+        }
+      }
+      if (GROUPED || !p.out_f32) {
+        named_barrier_sync(1, 128);
+        const int m_end = quarter * (BN2 / 4) + BN2 / 4;
+        for (int m = quarter * (BN2 / 4); m < m_end && m < rows_valid; ++m) {
+          const int64_t pos = row0 + m;
+          int64_t orow = pos;
+          if (GROUPED && p.scatter) orow = p.perm[pos];
+          uint2 v = *reinterpret_cast<const uint2 *>(staging + m * 128 + 4 * lane);
+          if (!GROUPED && p.residual) {
+            const uint2 rv = *reinterpret_cast<const uint2 *>(p.residual + pos * p.ldr + col0 + 4 * lane);
+            const uint16_t *hv = reinterpret_cast<const uint16_t *>(&v);
+            const uint16_t *hr = reinterpret_cast<const uint16_t *>(&rv);
+            uint16_t o4[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) o4[q] = f32_to_bf16(__fadd_rn(bf16_to_f32(hr[q]), bf16_to_f32(hv[q])));
+            v = *reinterpret_cast<uint2 *>(o4);
+          }
+          *reinterpret_cast<uint2 *>(p.out + orow * p.ldo + col0 + 4 * lane) = v;
+        }
+        named_barrier_sync(1, 128);
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still signal it
+  if (warp == MMA_W) {
+    tc_fence_after();
+    tmem_dealloc2(tmem, TMEM2_COLS);
+  }
+  if (threadIdx.x == 0 && s.err) atomicCAS(p.err, 0, s.err);
+}
+
+}  // namespace two_sm

@@ -100,8 +100,9 @@ __global__ void count_kernel(const float *__restrict__ routes, int64_t tokens, i
 
 // Single CTA: offsets (exclusive prefix), GEMM tile list (128-row tiles), and optionally
 // the reference-format counts groups[e][0] and 16-row task list.
-__global__ void scan_kernel(const int *__restrict__ counts, int experts, int64_t tokens, int *__restrict__ offsets,
-                            int *__restrict__ tile_list, float *__restrict__ groups, float *__restrict__ tasks) {
+__global__ void scan_kernel(const int *__restrict__ counts, int experts, int64_t tokens, int tile_rows,
+                            int *__restrict__ offsets, int *__restrict__ tile_list, float *__restrict__ groups,
+                            float *__restrict__ tasks) {
   __shared__ int s_off[1025], s_tiles[1025], s_tasks[1025];
   const int e = threadIdx.x;
   const int c = e < experts ? counts[e] : 0;
@@ -113,7 +114,7 @@ __global__ void scan_kernel(const int *__restrict__ counts, int experts, int64_t
       s_tiles[i] = trun;
       s_tasks[i] = krun;
       run += ci;
-      trun += (ci + 127) / 128;
+      trun += (ci + tile_rows - 1) / tile_rows;
       krun += (ci + 15) / 16;
     }
     s_off[experts] = run;
@@ -123,9 +124,9 @@ __global__ void scan_kernel(const int *__restrict__ counts, int experts, int64_t
   __syncthreads();
   if (e < experts) {
     offsets[e] = s_off[e];
-    for (int i = 0; i < (c + 127) / 128; ++i) {
+    for (int i = 0; i < (c + tile_rows - 1) / tile_rows; ++i) {
       tile_list[1 + 2 * (s_tiles[e] + i)] = e;
-      tile_list[2 + 2 * (s_tiles[e] + i)] = s_off[e] + 128 * i;
+      tile_list[2 + 2 * (s_tiles[e] + i)] = s_off[e] + tile_rows * i;
     }
     if (groups) groups[(int64_t)e * (tokens + 1)] = (float)c;
     if (tasks) {
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(256) fill_kernel(const float *__restrict__ rou
   }
 }
 
-int launch_group(const float *routes, int64_t tokens, int topk, int experts, int *counts, int *offsets,
+int launch_group(const float *routes, int64_t tokens, int topk, int experts, int tile_rows, int *counts, int *offsets,
                  int *tile_list, int *perm, float *groups, float *order, float *tasks, cudaStream_t stream,
                  int num_sms) {
   if (experts > 1024 || topk <= 0) return CLEFQ_ERR_SHAPE;
@@ -196,8 +197,8 @@ int launch_group(const float *routes, int64_t tokens, int topk, int experts, int
     int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 8;
     count_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(routes, tokens, topk, experts, counts);
   }
-  scan_kernel<<<1, experts <= 32 ? 32 : ((experts + 31) / 32) * 32, 0, stream>>>(counts, experts, tokens, offsets,
-                                                                                 tile_list, groups, tasks);
+  scan_kernel<<<1, experts <= 32 ? 32 : ((experts + 31) / 32) * 32, 0, stream>>>(counts, experts, tokens, tile_rows,
+                                                                                 offsets, tile_list, groups, tasks);
   if (tokens > 0)
     fill_kernel<<<experts, 256, 0, stream>>>(routes, tokens, topk, offsets, groups, order, perm);
   return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
@@ -234,7 +235,8 @@ int launch_tasks(const float *groups, int64_t tokens, int experts, float *tasks,
 
 // Sorted-layout tables from a reference-format groups buffer: offsets, perm, tile list.
 __global__ void groups_to_sorted_kernel(const float *__restrict__ groups, int64_t tokens, int topk, int experts,
-                                        int *__restrict__ offsets, int *__restrict__ perm, int *__restrict__ tile_list) {
+                                        int tile_rows, int *__restrict__ offsets, int *__restrict__ perm,
+                                        int *__restrict__ tile_list) {
   const int cap = (int)(tokens * topk);
   __shared__ int s_off[1025], s_tiles[1025], s_cnt[1024];
   if (threadIdx.x == 0) {
@@ -249,7 +251,7 @@ __global__ void groups_to_sorted_kernel(const float *__restrict__ groups, int64_
       s_off[e] = run;
       s_tiles[e] = trun;
       run += c;
-      trun += (c + 127) / 128;
+      trun += (c + tile_rows - 1) / tile_rows;
     }
     s_off[experts] = run;
     s_tiles[experts] = trun;
@@ -260,9 +262,9 @@ __global__ void groups_to_sorted_kernel(const float *__restrict__ groups, int64_
   for (int e = threadIdx.x; e < experts; e += blockDim.x) {
     const int c = s_cnt[e];
     offsets[e] = s_off[e];
-    for (int i = 0; i < (c + 127) / 128; ++i) {
+    for (int i = 0; i < (c + tile_rows - 1) / tile_rows; ++i) {
       tile_list[1 + 2 * (s_tiles[e] + i)] = e;
-      tile_list[2 + 2 * (s_tiles[e] + i)] = s_off[e] + 128 * i;
+      tile_list[2 + 2 * (s_tiles[e] + i)] = s_off[e] + tile_rows * i;
     }
   }
   __syncthreads();
@@ -275,10 +277,10 @@ __global__ void groups_to_sorted_kernel(const float *__restrict__ groups, int64_
   }
 }
 
-int launch_groups_to_sorted(const float *groups, int64_t tokens, int topk, int experts, int *offsets, int *perm,
-                            int *tile_list, cudaStream_t stream) {
+int launch_groups_to_sorted(const float *groups, int64_t tokens, int topk, int experts, int tile_rows, int *offsets,
+                            int *perm, int *tile_list, cudaStream_t stream) {
   if (experts > 1024) return CLEFQ_ERR_SHAPE;
-  groups_to_sorted_kernel<<<1, 256, 0, stream>>>(groups, tokens, topk, experts, offsets, perm, tile_list);
+  groups_to_sorted_kernel<<<1, 256, 0, stream>>>(groups, tokens, topk, experts, tile_rows, offsets, perm, tile_list);
   return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
 }
 

@@ -276,13 +276,13 @@ def _expert_weights(rng, experts, n, k):
 
 
 @pytest.mark.parametrize("tokens,skewed", [(1, False), (37, False), (300, True), (1000, False)])
-@pytest.mark.parametrize("routed", [False, True])
-def test_expert_matches_oracle(cq, tokens, skewed, routed):
-    """Grouped INT4 experts, bit-exact (src/benchmarking/omni.rs:176-345 fixtures)."""
+@pytest.mark.parametrize("routed,k,n", [(False, 512, 256), (True, 256, 512), (False, 256, 384), (True, 256, 384)])
+def test_expert_matches_oracle(cq, tokens, skewed, routed, k, n):
+    """Grouped INT4 experts, bit-exact (src/benchmarking/omni.rs:176-345 fixtures); n=384
+    runs the one-CTA kernel, multiples of 256 the CTA-pair kernel."""
     from tests.golden.make_golden import expert_routes
     rng = np.random.default_rng(tokens)
     experts, topk = 128, 8
-    k, n = (256, 512) if routed else (512, 256)
     wt, ws, wdev = _expert_weights(rng, experts, n, k)
     routes = expert_routes(tokens, skewed, 0)
     groups, _ = o.group(routes)
