@@ -299,6 +299,13 @@ CQ_DEV void tma_load_2d_cg2(void *dst, const void *desc, uint32_t bar, int x, in
       "l"(desc), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
+CQ_DEV void tma_load_3d_cg2(void *dst, const void *desc, uint32_t bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(desc), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 CQ_DEV void tmem_alloc2(uint32_t *slot_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
                "r"(ncols)

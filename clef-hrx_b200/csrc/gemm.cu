@@ -388,6 +388,19 @@ static bool weight_map(EncodeTiledFn enc, CUtensorMap *m, const uint32_t *w, int
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The same weight tiles with one box = one whole block (int4) or two consecutive blocks
+// (int8): 16 or 32 KB contiguous, 128-byte swizzled.
+static bool weight_map_blocks(EncodeTiledFn enc, CUtensorMap *m, const uint32_t *w, int64_t rows, int k, int bits) {
+  const int64_t blocks = rows / 128 * (k / (32 * (32 / bits)));
+  cuuint64_t dims[3] = {32, 128, (cuuint64_t)blocks};
+  cuuint64_t strides[2] = {128, 16384};
+  cuuint32_t box[3] = {32, 128, (cuuint32_t)(bits == 4 ? 1 : 2)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint32_t *>(w), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <bool G, int B>
 static void launch_variant(dim3 grid, const CUtensorMap &t, const CUtensorMap &w0, const CUtensorMap &w1,
                            const GemmParams &p, cudaStream_t stream) {
@@ -469,6 +482,22 @@ int launch_gemm(const GemmParams &p, cudaStream_t stream) {
     wmap1 = wmap0;
   }
   if (pairs) {
+    // token operand as 3D: x = 128 bytes of a K slice, y = rows (pitch a_ld), z = K slices
+    cuuint64_t d3[3] = {128, (cuuint64_t)p.a_rows, (cuuint64_t)(p.k / 128)};
+    cuuint64_t s3[2] = {(cuuint64_t)p.a_ld, 128};
+    cuuint32_t b3[3] = {128, (cuuint32_t)two_sm::HALF, 2};
+    cuuint32_t e3[3] = {1, 1, 1};
+    if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(p.a_op), d3, s3, b3, e3,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return CLEFQ_ERR_CUDA;
+    // weights: whole 128-row x 32-word blocks (int8: the two blocks of a K=256 slice)
+    if (!weight_map_blocks(enc, &wmap0, p.w[0], wrows, p.k, p.bits)) return CLEFQ_ERR_CUDA;
+    if (two) {
+      if (!weight_map_blocks(enc, &wmap1, p.w[1], wrows, p.k, p.bits)) return CLEFQ_ERR_CUDA;
+    } else {
+      wmap1 = wmap0;
+    }
     const int64_t pair_tiles = tiles_m * (p.n / two_sm::BMP);
     cudaError_t e;
     if (p.grouped)

@@ -11,8 +11,11 @@
 //     completion (tcgen05.commit) to both CTAs,
 //   * both CTAs drain their 128-row slice of the accumulator; accumulators are double
 //     buffered (2 x 192 TMEM columns) so a tile's epilogue overlaps the next mainloop.
-// Per SM this moves 20 KB of operands per 384 MMA cycles (~53 B/clk), under the ~67 B/clk
-// the L2 delivers to one SM, where the 128 x 128 one-CTA tile needs ~96 B/clk.
+// Per SM this moves 40 KB of operands per 768 MMA cycles (~53 B/clk), under the ~67 B/clk
+// the L2 delivers to one SM, where the 128 x 128 one-CTA tile needs ~96 B/clk.  Each
+// K=256 stage is exactly two TMA boxes (a 24 KB 3D token box holding two 128-byte K
+// slices, and one contiguous 16 KB weight block): an SM's TMA unit completes about one
+// box per ~250 cycles whatever its size up to 16 KB, so small boxes cap the feed rate.
 #pragma once
 
 namespace two_sm {
@@ -20,20 +23,21 @@ namespace two_sm {
 constexpr int BMP = 256;                       // weight rows per pair tile (128 per CTA)
 constexpr int BN2 = 192;                       // tokens per pair tile (96 per CTA)
 constexpr int HALF = 96;                       // token rows held by one CTA
-constexpr int KS2 = 128;                       // codes per stage
-constexpr int TOK_B = HALF * KS2;              // 12 KiB
-constexpr int NSW = 4;                         // TMEM weight stages
+constexpr int KS2 = 256;                       // codes per stage
+constexpr int TOK_B = HALF * KS2;              // 24 KiB: two 12 KiB K-slices of 96 rows
+constexpr int NSW = 2;                         // TMEM weight stages (64 columns each)
 constexpr int ACC_COLS = 192;
 constexpr int WCOL = 2 * ACC_COLS;             // 384: weight stages after both accumulators
 constexpr int TMEM2_COLS = 512;
-constexpr int THREADS2 = 320;                  // 4 converter, 1 TMA, 1 MMA, 4 epilogue warps
+constexpr int THREADS2 = 448;                  // 4 converter, 1 TMA, 1 MMA, 8 epilogue warps
+constexpr int EPI_WARPS = 8;                   // two per TMEM lane quarter, 96 tokens each
 constexpr int TMA_W = 4, MMA_W = 5;
 constexpr uint32_t IDESC2 = idesc_i8(256, BN2);
 constexpr int STAGING2 = BN2 * 128 * 2;        // 48 KiB BF16 [token][column]
 
 template <int BITS>
 struct Cfg2 {
-  static constexpr int NS = BITS == 4 ? 8 : 6;
+  static constexpr int NS = BITS == 4 ? 4 : 3;
   static constexpr int W_BYTES = 128 * KS2 * BITS / 8;
   static constexpr int STAGE = TOK_B + W_BYTES;
   static constexpr int SMEM = NS * STAGE + STAGING2 + 1024 + 1024;
@@ -43,7 +47,7 @@ template <int NS>
 struct Smem2 {
   uint64_t tok_full[NS], tok_empty[NS], wsm_full[NS], wsm_empty[NS];
   uint64_t wtm_full[NSW], wtm_empty[NSW], acc_full[2], acc_empty[2];
-  uint32_t sink[8];  // targets of the follower's asynchronous 4-byte signals
+  uint32_t sink[4 + EPI_WARPS];  // targets of the follower's asynchronous 4-byte signals
   uint32_t tmem_base;
   int err;
 };
@@ -105,7 +109,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
-      mbar_init(&s.acc_empty[i], 4);
+      mbar_init(&s.acc_empty[i], EPI_WARPS);
     }
     s.err = 0;
     fence_barrier_init();
@@ -153,13 +157,12 @@ __global__ void __launch_bounds__(THREADS2, 1)
             break;
           uint8_t *stage = ring + st * C::STAGE;
           if (rank == 0) mbar_arrive_expect_tx(&s.tok_full[st], 2 * TOK_B);
-          tma_load_2d_cg2(stage, &tok_map, mapa_shared(smem_u32(&s.tok_full[st]), 0), kb * KS2,
-                          (int)(row0 + HALF * rank));
+          // token box: x = 128 bytes of a K slice, y = 96 rows, z = the stage's two K slices
+          tma_load_3d_cg2(stage, &tok_map, mapa_shared(smem_u32(&s.tok_full[st]), 0), 0, (int)(row0 + HALF * rank),
+                          2 * kb);
           mbar_arrive_expect_tx(&s.wsm_full[st], C::W_BYTES);
-          if (BITS == 4)
-            tma_load_3d(stage + TOK_B, w_map, &s.wsm_full[st], (kb & 1) * 16, 0, w_row_tile * blocks_k + (kb >> 1));
-          else
-            tma_load_3d(stage + TOK_B, w_map, &s.wsm_full[st], 0, 0, w_row_tile * blocks_k + kb);
+          // weight box: whole 128-row x 32-word tiled block(s) of this K=256 slice
+          tma_load_3d(stage + TOK_B, w_map, &s.wsm_full[st], 0, 0, w_row_tile * blocks_k + kb * (BITS == 4 ? 1 : 2));
         }
       }
     }
@@ -186,7 +189,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
           const uint32_t b_base = smem_u32(ring + st * C::STAGE);
 #pragma unroll
           for (int j = 0; j < KS2 / 32; ++j)
-            mma_i8_ts2(acc, tmem + WCOL + 32 * sw + 8 * j, smem_desc_sw128(b_base + 32 * j), IDESC2, (kb | j) != 0);
+            mma_i8_ts2(acc, tmem + WCOL + 64 * sw + 8 * j, smem_desc_sw128(b_base + (j >> 2) * (TOK_B / 2) + 32 * (j & 3)),
+                       IDESC2, (kb | j) != 0);
           mma_commit2_mc(&s.tok_empty[st], 3);
           mma_commit2_mc(&s.wtm_empty[sw], 3);
         }
@@ -216,32 +220,41 @@ __global__ void __launch_bounds__(THREADS2, 1)
         if (!(ok = waited)) break;
         tc_fence_after();
         const uint32_t wbase = smem_u32(ring + st * C::STAGE + TOK_B);
-        uint32_t o[32];
-        if (BITS == 4) {
-          uint32_t w[16];
+        // 128-byte rows, 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
+        uint32_t w[32];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 v = lds_v4(wbase + r * 64 + 16 * (c ^ ((r >> 1) & 3)));
-            w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
-          }
-          mbar_arrive(&s.wsm_empty[st]);
-#pragma unroll
-          for (int gq = 0; gq < 4; ++gq) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              o[8 * gq + q] = nib_lo16(w[4 * gq + q]);
-              o[8 * gq + 4 + q] = nib_hi16(w[4 * gq + q]);
-            }
-          }
-        } else {
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = lds_v4(wbase + r * 128 + 16 * (c ^ (r & 7)));
+          w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+        }
+        uint32_t w2[32];
+        if (BITS == 8) {
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            const uint4 v = lds_v4(wbase + r * 128 + 16 * (c ^ (r & 7)));
-            o[4 * c] = v.x; o[4 * c + 1] = v.y; o[4 * c + 2] = v.z; o[4 * c + 3] = v.w;
+            const uint4 v = lds_v4(wbase + 16384 + r * 128 + 16 * (c ^ (r & 7)));
+            w2[4 * c] = v.x; w2[4 * c + 1] = v.y; w2[4 * c + 2] = v.z; w2[4 * c + 3] = v.w;
           }
-          mbar_arrive(&s.wsm_empty[st]);
         }
-        tmem_st_x32(tmem + lane_base + WCOL + 32 * sw, o);
+        mbar_arrive(&s.wsm_empty[st]);
+        if (BITS == 4) {
+          // 8 words per 32-code group -> low nibbles then high nibbles (x16)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t o[32];
+#pragma unroll
+            for (int gq = 0; gq < 4; ++gq) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                o[8 * gq + q] = nib_lo16(w[16 * h + 4 * gq + q]);
+                o[8 * gq + 4 + q] = nib_hi16(w[16 * h + 4 * gq + q]);
+              }
+            }
+            tmem_st_x32(tmem + lane_base + WCOL + 64 * sw + 32 * h, o);
+          }
+        } else {
+          tmem_st_x32(tmem + lane_base + WCOL + 64 * sw, w);
+          tmem_st_x32(tmem + lane_base + WCOL + 64 * sw + 32, w2);
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -256,50 +269,61 @@ __global__ void __launch_bounds__(THREADS2, 1)
       }
     }
   } else {
-    // ---- epilogue (warps 6-9, both CTAs): this CTA's 128 weight rows x 192 tokens -------
+    // ---- epilogue (warps 6-13, both CTAs): this CTA's 128 weight rows x 192 tokens ------
+    // Warp e covers TMEM lane quarter (warp & 3) and tokens [96*half, 96*half + 96).
+    // Activation scales (and routes) of the next tile are fetched before its accumulator
+    // is ready, so their global-load latency overlaps the mainloop.
     const int quarter = warp & 3;
+    const int ehalf = (warp - 6) >> 2;
+    const int eidx = warp - 6;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t lead_acc_empty = mapa_shared(smem_u32(&s.acc_empty[0]), 0);
-    const uint32_t lead_sink = mapa_shared(smem_u32(&s.sink[4 + quarter]), 0);
+    const uint32_t lead_sink = mapa_shared(smem_u32(&s.sink[4 + eidx]), 0);
     const int shift = BITS == 4 ? 8 : 0;
     const float big = 3.3895313892515355e38f;
+    constexpr int CH = (BN2 / 2) / 32;  // 32-token chunks per warp
     int i = 0;
     int64_t row0;
     int rows_valid, np, expert;
     for (int t = cluster; tm.get(p, t, row0, rows_valid, np, expert); t += nclusters, ++i) {
       const int buf = i & 1;
-      bool have = true;
-      if (lane == 0) have = mbar_wait_bounded(&s.acc_full[buf], (i >> 1) & 1, &s.err, 5);
-      have = __shfl_sync(0xffffffffu, have, 0) != 0;
-      if (!named_barrier_and(2, 128, have)) break;
-      tc_fence_after();
-      int which, w_row_tile;
-      weight_tile(np, expert, which, w_row_tile);
-      const float ws = p.w_scales[which][(int64_t)w_row_tile * 128 + r];
-      const int col0 = (2 * np + (int)rank) * 128;  // first output column of this CTA
-#pragma unroll 1
-      for (int c = 0; c < BN2; c += 32) {
-        uint32_t accv[32];
-        tmem_ld_x32(tmem + lane_base + ACC_COLS * buf + c, accv);
-        const int mj = c + lane;
-        float my_scale = 0.0f;
+      float my_scale[CH];
+#pragma unroll
+      for (int q = 0; q < CH; ++q) {
+        const int mj = ehalf * (BN2 / 2) + 32 * q + lane;
+        my_scale[q] = 0.0f;
         if (mj < rows_valid) {
           const int64_t pos = row0 + mj;
           if (GROUPED) {
             const int64_t route = p.perm[pos];
-            my_scale = p.a_scales[p.scale_mode == 0 ? pos : (p.scale_mode == 1 ? route / p.topk : route)];
+            my_scale[q] = p.a_scales[p.scale_mode == 0 ? pos : (p.scale_mode == 1 ? route / p.topk : route)];
           } else {
-            my_scale = p.a_scales[pos];
+            my_scale[q] = p.a_scales[pos];
           }
         }
+      }
+      int which, w_row_tile;
+      weight_tile(np, expert, which, w_row_tile);
+      const float ws = p.w_scales[which][(int64_t)w_row_tile * 128 + r];
+      const int col0 = (2 * np + (int)rank) * 128;  // first output column of this CTA
+      bool have = true;
+      if (lane == 0) have = mbar_wait_bounded(&s.acc_full[buf], (i >> 1) & 1, &s.err, 5);
+      have = __shfl_sync(0xffffffffu, have, 0) != 0;
+      if (!named_barrier_and(2, 32 * EPI_WARPS, have)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int q = 0; q < CH; ++q) {
+        const int c = ehalf * (BN2 / 2) + 32 * q;
+        uint32_t accv[32];
+        tmem_ld_x32(tmem + lane_base + ACC_COLS * buf + c, accv);
         tmem_ld_wait();
-        if (c + 32 >= BN2) {
+        if (q == CH - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
             if (rank == 0) {
-              if (quarter == 0) mbar_arrive_expect_tx(&s.acc_empty[buf], 16);
+              if (eidx == 0) mbar_arrive_expect_tx(&s.acc_empty[buf], 4 * EPI_WARPS);
               else mbar_arrive(&s.acc_empty[buf]);
             } else {
               st_async_signal(lead_sink, lead_acc_empty + 8 * buf);
@@ -308,7 +332,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float as = __shfl_sync(0xffffffffu, my_scale, j);
+          const float as = __shfl_sync(0xffffffffu, my_scale[q], j);
           const float a = __int2float_rn((int)accv[j] >> shift);
           uint16_t h;
           if (GROUPED) {
@@ -326,9 +350,10 @@ __global__ void __launch_bounds__(THREADS2, 1)
         }
       }
       if (GROUPED || !p.out_f32) {
-        named_barrier_sync(1, 128);
-        const int m_end = quarter * (BN2 / 4) + BN2 / 4;
-        for (int m = quarter * (BN2 / 4); m < m_end && m < rows_valid; ++m) {
+        named_barrier_sync(1, 32 * EPI_WARPS);
+        // each warp stores 24 token rows, 256 contiguous bytes per row
+        const int m_end = eidx * (BN2 / EPI_WARPS) + BN2 / EPI_WARPS;
+        for (int m = eidx * (BN2 / EPI_WARPS); m < m_end && m < rows_valid; ++m) {
           const int64_t pos = row0 + m;
           int64_t orow = pos;
           if (GROUPED && p.scatter) orow = p.perm[pos];
@@ -339,12 +364,12 @@ __global__ void __launch_bounds__(THREADS2, 1)
             const uint16_t *hr = reinterpret_cast<const uint16_t *>(&rv);
             uint16_t o4[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) o4[q] = f32_to_bf16(__fadd_rn(bf16_to_f32(hr[q]), bf16_to_f32(hv[q])));
+            for (int qq = 0; qq < 4; ++qq) o4[qq] = f32_to_bf16(__fadd_rn(bf16_to_f32(hr[qq]), bf16_to_f32(hv[qq])));
             v = *reinterpret_cast<uint2 *>(o4);
           }
           *reinterpret_cast<uint2 *>(p.out + orow * p.ldo + col0 + 4 * lane) = v;
         }
-        named_barrier_sync(1, 128);
+        named_barrier_sync(1, 32 * EPI_WARPS);
       }
     }
   }
