@@ -34,6 +34,7 @@ _SYMBOLS = {
     "clefq_gemm_workspace_size": (ctypes.c_int64, ["l", "l", "i"]),
     "clefq_gemm": (ctypes.c_int, ["p", "i", "p", "l", "p", "l", "p", "p", "l", "l", "p", "l", "i", "p", "l", "p", "l"]),
     "clefq_gemm_s8": (ctypes.c_int, ["p", "i", "p", "l", "p", "l", "p", "p", "l", "l", "p", "l", "i", "p", "l"]),
+    "clefq_gemm_noalloc": (ctypes.c_int, ["p", "p", "l", "p", "l", "p", "p", "l", "l", "p", "l", "i", "p", "l"]),
     "clefq_swiglu": (ctypes.c_int, ["p", "p", "p", "l", "p"]),
     "clefq_route": (ctypes.c_int, ["p", "p", "i", "l", "i", "i", "p"]),
     "clefq_group_workspace_size": (ctypes.c_int64, ["l", "i", "i"]),

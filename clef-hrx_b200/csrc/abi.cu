@@ -71,6 +71,9 @@ int64_t aligned_total(const Arena &a) { return (a.used + 255) & ~int64_t(255); }
 bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 }  // namespace
 
+// Records a failure message for clefq_last_error() from another translation unit.
+int report_error(int code, const char *msg) { return set_err(code, "%s", msg); }
+
 int device_sms() {
   const int d = current_device();
   std::lock_guard<std::mutex> lk(g_mu);

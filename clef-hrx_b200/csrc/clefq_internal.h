@@ -69,6 +69,7 @@ int launch_gemm(const GemmParams &p, cudaStream_t stream);
 int gemm_tile_rows(int n, int n_split);
 
 int device_sms();
+int report_error(int code, const char *msg);  // sets clefq_last_error()
 int *device_status_word();  // per-device zero-initialised status word used by bounded waits
 
 }  // namespace cq

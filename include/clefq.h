@@ -108,6 +108,25 @@ CLEFQ_API int clefq_gemm(void *stream, int bits, const void *a_codes, int64_t a_
                          int64_t m, const void *w_tiled, const float *w_scales, int64_t n, int64_t k,
                          const void *residual, int64_t residual_ld, int out_dtype, void *out, int64_t out_ld,
                          void *workspace, int64_t workspace_bytes);
+/*
+ * The same projection as clefq_gemm (bits 4 only) for callers that cannot allocate device
+ * memory and so cannot pass a workspace: for example a host runtime that reserves all of
+ * device memory for its own allocator at start-up and gives a plugin nothing but each
+ * call's inputs and outputs, or an FFI binding with no workspace argument.  It has no
+ * counterpart in the reference (whose engine owns every allocation).
+ * The s8 operand scratch is a fixed 64 MiB array inside this library's device image:
+ *   - m * k must be <= CLEFQ_GEMM_NOALLOC_MAX_BYTES, else CLEFQ_ERR_WORKSPACE;
+ *   - every GPU on which it has been used keeps those 64 MiB until the process exits;
+ *   - all calls on a device share the array, so calls that overlap on the GPU (other
+ *     streams or host threads) race on it -- the caller must serialise them;
+ *   - the first call on a device resolves the array's address with that device current.
+ * Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
+ */
+#define CLEFQ_GEMM_NOALLOC_MAX_BYTES (64ll << 20)
+CLEFQ_API int clefq_gemm_noalloc(void *stream, const void *a_codes, int64_t a_ld_words, const float *a_scales,
+                                 int64_t m, const void *w_tiled, const float *w_scales, int64_t n, int64_t k,
+                                 const void *residual, int64_t residual_ld, int out_dtype, void *out, int64_t out_ld);
+
 /* Same projection from an s8 operand written by clefq_prepare (no unpack pass). */
 CLEFQ_API int clefq_gemm_s8(void *stream, int bits, const void *operand, int64_t operand_ld, const float *a_scales,
                             int64_t m, const void *w_tiled, const float *w_scales, int64_t n, int64_t k,
