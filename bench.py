@@ -158,13 +158,17 @@ def rand_weight_host(rng, rows, cols):
     return codes, scales, rows
 
 
-def time_steps(fn, steps, flush):
+def time_steps(fn, steps, flush, lead_cycles=0):
     """Device time of each step (CUDA events on the launching stream), L2 flushed before
-    every step; returns per-step milliseconds."""
+    every step; returns per-step milliseconds.  lead_cycles > 0 queues a GPU spin after
+    the flush so the host has enqueued the step before its start event executes: a
+    kernel shorter than the host's launch path is then timed, not the host."""
     stream = torch.cuda.current_stream()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for a, b in evs:
         flush.fill_(1)
+        if lead_cycles:
+            torch.cuda._sleep(lead_cycles)
         a.record(stream)
         fn()
         b.record(stream)
@@ -277,11 +281,15 @@ def run_clefq(args, world, rank, local):
         clefq._call("clefq_gemm_s8", clefq._stream(), 4, clefq._ptr(hid.operand), INTER, clefq._ptr(hid.scales), M,
                     clefq._ptr(down.codes), clefq._ptr(down.scales), HIDDEN, INTER, None, 0, 0, clefq._ptr(out),
                     HIDDEN)
+    lead = 400_000   # ~0.2 ms of GPU spin ahead of each timed kernel
     for name, fn in (("gemm_gate", gemm_gu), ("gemm_down", gemm_down)):
         fn()
-        ktimes[name] = statistics.median(time_steps(fn, reps, flush))
+        ktimes[name] = statistics.median(time_steps(fn, reps, flush, lead))
     ktimes["prepare_x"] = statistics.median(time_steps(lambda: clefq.prepare(x, 4, clefq.stride_for(HIDDEN)), reps,
-                                                       flush))
+                                                       flush, lead))
+    ktimes["prepare_swiglu"] = statistics.median(time_steps(
+        lambda: clefq.prepare(gu[:, :INTER], 4, INTER + (128 if INTER % 1024 == 0 else 0), clefq.PREP_SWIGLU,
+                              gu[:, INTER:]), reps, flush, lead))
     # Roofline of the down projection exactly as clefq_mlp launches it (M=4096, N=4096,
     # K=12288): the ncu capture in profiles/ is of that launch.  Algorithmic work 2*M*N*K.
     gemm_ops = 2.0 * M * HIDDEN * INTER

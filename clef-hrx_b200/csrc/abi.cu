@@ -146,8 +146,7 @@ static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_
   a.op_ld = operand_ld;
   a.norm_out = static_cast<uint16_t *>(norm_out);
   a.norm_ld = norm_ld;
-  rc = launch_prepare(a, s);
-  return rc ? cuda_err("prepare launch") : 0;
+  return launch_prepare(a, s);  // sets clefq_last_error() itself on failure
 }
 
 static int run_gemm(cudaStream_t s, int bits, const uint8_t *op, int64_t op_ld, int64_t op_rows, const float *a_scales,

@@ -7,52 +7,11 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include "cq_math.h"
 
 #define CQ_DEV __device__ __forceinline__
 
 namespace cq {
-
-// ---------------------------------------------------------------------------------------
-// BF16 <-> F32, round to nearest even (the reference's `half` crate and Loom fptrunc);
-// NaN keeps its sign and top payload bits with the quiet bit set.
-// ---------------------------------------------------------------------------------------
-CQ_DEV float bf16_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
-CQ_DEV uint16_t f32_to_bf16(float f) {
-  uint32_t u = __float_as_uint(f);
-  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x0040u);
-  u += 0x7fffu + ((u >> 16) & 1u);
-  return (uint16_t)(u >> 16);
-}
-CQ_DEV float bf16r(float f) { return bf16_to_f32(f32_to_bf16(f)); }
-
-// exp(x): Cody & Waite (1980) two-constant argument reduction x = n ln2 + r, |r| <= ln2/2,
-// degree-7 Taylor polynomial of e^r in Horner form with fused multiply-adds, and exact
-// scaling by 2^n split into two powers of two.  Error below 2 ulp over the normal range;
-// the CPU oracle evaluates the identical steps, so the two agree bit for bit.
-CQ_DEV float pow2i(int n) { return __uint_as_float((uint32_t)(n + 127) << 23); }
-CQ_DEV float exp_cw(float x) {
-  if (x != x) return x;
-  if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
-  if (x < -103.972084045410156f) return 0.0f;
-  const float log2e = 1.44269502162933349609375f;
-  const float ln2_hi = 0.693145751953125f;
-  const float ln2_lo = 1.428606765330187045e-06f;
-  float n = rintf(__fmul_rn(x, log2e));
-  float r = __fmaf_rn(-n, ln2_hi, x);
-  r = __fmaf_rn(-n, ln2_lo, r);
-  float p = 1.0f / 5040.0f;
-  p = __fmaf_rn(p, r, 1.0f / 720.0f);
-  p = __fmaf_rn(p, r, 1.0f / 120.0f);
-  p = __fmaf_rn(p, r, 1.0f / 24.0f);
-  p = __fmaf_rn(p, r, 1.0f / 6.0f);
-  p = __fmaf_rn(p, r, 0.5f);
-  p = __fmaf_rn(p, r, 1.0f);
-  p = __fmaf_rn(p, r, 1.0f);
-  int ni = (int)n;
-  int n1 = ni / 2;
-  int n2 = ni - n1;
-  return __fmul_rn(__fmul_rn(p, pow2i(n1)), pow2i(n2));
-}
 
 // IEEE maxNum / minNum (return the non-NaN operand).
 CQ_DEV float maxnum(float a, float b) { return fmaxf(a, b); }

@@ -404,10 +404,12 @@ static bool weight_map_blocks(EncodeTiledFn enc, CUtensorMap *m, const uint32_t 
 template <bool G, int B>
 static void launch_variant(dim3 grid, const CUtensorMap &t, const CUtensorMap &w0, const CUtensorMap &w1,
                            const GemmParams &p, cudaStream_t stream) {
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[64];  // per device: the shared-memory limit is a per-context attribute
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr[dev]) {
     cudaFuncSetAttribute(gemm_i8_kernel<G, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<B>::SMEM);
-    attr = true;
+    if (dev >= 0 && dev < 64) attr[dev] = true;
   }
   gemm_i8_kernel<G, B><<<grid, THREADS, Cfg<B>::SMEM, stream>>>(t, w0, w1, p);
 }
@@ -417,7 +419,11 @@ template <bool G, int B>
 static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, const CUtensorMap &w0,
                                       const CUtensorMap &w1, const GemmParams &p, cudaStream_t stream) {
   using namespace two_sm;
-  static int max_clusters = 0;
+  static int max_clusters_dev[64];  // per device, like the shared-memory attribute
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int scratch = 0;
+  int &max_clusters = (dev >= 0 && dev < 64) ? max_clusters_dev[dev] : scratch;
   auto kern = gemm_i8_2sm_kernel<G, B>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

@@ -12,11 +12,11 @@
 //   unpack    packed int4 activation codes -> s8 GEMM operand (no reference counterpart:
 //             the operand format of the tcgen05 GEMM)
 //
-// Layout of one row in registers: a warp owns a 256-element Hadamard group, each lane
-// eight consecutive elements.  Radix-4 stride 1 runs inside a lane; strides 4, 16 and 64
-// exchange partial sums/differences with xor-shuffles, keeping the reference's exact
-// operation order (s01 = a+b, s23 = c+d, d01 = a-b, d23 = c-d; o = s01+d23, s01-d23,
-// d01+s23, s23-d01), which is bit-identical under IEEE commutativity.
+// Layout of one row in registers: a warp owns Hadamard groups of 256 elements, each lane
+// eight consecutive elements of a group.  Radix-4 stride 1 runs inside a lane; strides 4,
+// 16 and 64 exchange partial sums/differences with xor-shuffles.  The reference's
+// operation order is kept (s01 = a+b, s23 = c+d, d01 = a-b, d23 = c-d; o = s01+d23,
+// s01-d23, d01+s23, s23-d01), bit-identical under IEEE round-to-nearest-even.
 #include "cq_common.cuh"
 #include "clefq_internal.h"
 
@@ -24,28 +24,31 @@ namespace cq {
 
 enum { MODE_PLAIN = 0, MODE_SWIGLU = 1, MODE_ATTN_GATE = 2, MODE_NORM = 3, MODE_NORM_STORE = 4 };
 
-
 // One radix-4 stage across lanes.  Lane bits (xbit, ybit) select the element's role in
-// the quad (a: 0,0  b: 1,0  c: 0,1  d: 1,1).
-CQ_DEV void radix4_lanes(float (&v)[8], int lane, int xmask, int ymask) {
-  const bool bx = (lane & xmask) != 0;
+// the quad (a: 0,0  b: 1,0  c: 0,1  d: 1,1).  Every lane computes s = own + peer_x and
+// t = own - peer_x, then adds the t of its y-partner:
+//   a: (a+b) + (c-d) = s01 + d23        b: (a+b) + (d-c) = s01 - d23
+//   c: (c+d) + (a-b) = d01 + s23        d: (c+d) + (b-a) = s23 - d01
+// which are the reference's rounded results because x - y = -(y - x) and s + (-t) = s - t
+// exactly under round-to-nearest-even.  Only the sign of an exact zero can differ, and no
+// code or row scale depends on it.
+CQ_DEV void radix4_lanes(float (&v)[8], int xmask, int ymask) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    float own = v[i];
-    float peer = __shfl_xor_sync(0xffffffffu, own, xmask);
-    float s = __fadd_rn(own, peer);                              // a+b or c+d
-    float d = bx ? __fsub_rn(peer, own) : __fsub_rn(own, peer);  // a-b or c-d
-    float p2 = __shfl_xor_sync(0xffffffffu, d, ymask);
-    v[i] = bx ? __fsub_rn(s, p2) : __fadd_rn(s, p2);
+    const float own = v[i];
+    const float peer = __shfl_xor_sync(0xffffffffu, own, xmask);
+    const float s = __fadd_rn(own, peer);
+    const float t = __fsub_rn(own, peer);
+    v[i] = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, t, ymask));
   }
 }
 
-CQ_DEV void hadamard256_lane(float (&v)[8], int lane) {
+CQ_DEV void hadamard256_lane(float (&v)[8]) {
   // stride 1: two quads inside the lane
 #pragma unroll
   for (int q = 0; q < 8; q += 4) {
-    float a = v[q], b = v[q + 1], c = v[q + 2], d = v[q + 3];
-    float s01 = __fadd_rn(a, b), s23 = __fadd_rn(c, d), d01 = __fsub_rn(a, b), d23 = __fsub_rn(c, d);
+    const float a = v[q], b = v[q + 1], c = v[q + 2], d = v[q + 3];
+    const float s01 = __fadd_rn(a, b), s23 = __fadd_rn(c, d), d01 = __fsub_rn(a, b), d23 = __fsub_rn(c, d);
     v[q] = __fadd_rn(s01, d23);
     v[q + 1] = __fsub_rn(s01, d23);
     v[q + 2] = __fadd_rn(d01, s23);
@@ -54,191 +57,455 @@ CQ_DEV void hadamard256_lane(float (&v)[8], int lane) {
   // stride 4: (a, b) = (v[i], v[i+4]) of the even lane, (c, d) of the odd lane
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float x = v[i], y = v[i + 4];
-    float s = __fadd_rn(x, y), d = __fsub_rn(x, y);
-    float p2 = __shfl_xor_sync(0xffffffffu, d, 1);
+    const float x = v[i], y = v[i + 4];
+    const float s = __fadd_rn(x, y), d = __fsub_rn(x, y);
+    const float p2 = __shfl_xor_sync(0xffffffffu, d, 1);
     v[i] = __fadd_rn(s, p2);
     v[i + 4] = __fsub_rn(s, p2);
   }
-  radix4_lanes(v, lane, 2, 4);    // stride 16
-  radix4_lanes(v, lane, 8, 16);   // stride 64
+  radix4_lanes(v, 2, 4);    // stride 16
+  radix4_lanes(v, 8, 16);   // stride 64
 }
 
-template <int CH>
-__global__ void __launch_bounds__(512) prepare_kernel(PrepareArgs p) {
-  extern __shared__ float red[];  // [rows_per_block][team_warps] maxima, then norm partials
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int team = warp / p.team_warps, wt = warp % p.team_warps;
-  const int64_t row = (int64_t)blockIdx.x * p.rows_per_block + team;
-  const bool row_ok = row < p.rows;
-  const int ngroups = p.width >> 8;
-  const int bits = p.bits;
-  const int P = 32 / bits;
-  const int words = p.stride / P;
-  const uint16_t *xr = p.x + (row_ok ? row : 0) * p.x_ld;
+// Two products rounded to BF16 by one cvt.rn.bf16x2 and widened back to F32.  Finite and
+// infinite values round exactly like f32_to_bf16; a NaN may lose its payload, which the
+// packing never observes (a non-finite row packs to zero codes with an infinite scale).
+CQ_DEV void bf16r_pair(float &lo, float &hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  lo = __uint_as_float(r << 16);
+  hi = __uint_as_float(r & 0xffff0000u);
+}
 
-  // RMSNorm: 256 strided partial sums -> warp butterflies -> warp totals in order.
-  float norm_inv = 1.0f;
-  if (p.mode == MODE_NORM || p.mode == MODE_NORM_STORE) {
-    float s = 0.0f;
-    for (int j = threadIdx.x; j < p.width; j += 256) {
-      float v = bf16_to_f32(xr[j]);
-      s = __fmaf_rn(v, v, s);
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-    float *wsum = red + p.rows_per_block * p.team_warps;
-    if (lane == 0) wsum[warp] = s;
-    __syncthreads();
-    float total = wsum[0];
-    for (int w = 1; w < 8; ++w) total = __fadd_rn(total, wsum[w]);
-    float var = __fdiv_rn(total, (float)p.width);
-    norm_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-6f)));
-  }
+// max(m, |a|, |b|) propagating NaN (PTX max.NaN), so one non-finite element poisons the row.
+CQ_DEV float absmax3_nan(float m, float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
+  return r;
+}
+CQ_DEV float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
 
-  float v[CH][8];
-  float m = 0.0f;
+// Round to the nearest integer, ties to even (cvt.rni), as the reference's rint().
+CQ_DEV int rint_s32(float x) {
+  int r;
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+// Packs a pair of codes below the low bits of c: (c << 2w) | (hi << w) | lo, each code
+// saturated to the signed w-bit range (cvt.pack.sat).  For a finite row every code lies in
+// [-qmax, qmax]: scale = R/16/qmax and inv = 0.0625/scale are each rounded once, so
+// |x * inv| <= qmax (1 + 3 * 2^-24) < qmax + 0.5 for |x| <= R, and the saturation never
+// acts -- it equals the reference's clamp to +-qmax.
+CQ_DEV uint32_t pack_s4(int hi, int lo, uint32_t c) {
+  uint32_t r;
+  asm("cvt.pack.sat.s4.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(hi), "r"(lo), "r"(c));
+  return r;
+}
+CQ_DEV uint32_t pack_s8(int hi, int lo, uint32_t c) {
+  uint32_t r;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(hi), "r"(lo), "r"(c));
+  return r;
+}
+
+// bf16(silu(g)) for every BF16 bit pattern g, generated at build time by gen_tables.cpp
+// with the arithmetic of cq_math.h (identical to silu_bf16() evaluated on the device).
+constexpr int kSiluEntries = 65536;
+__device__ const uint16_t g_silu_bf16[kSiluEntries] __align__(16) = {
+#include "silu_bf16.inc"
+};
+
+// KIND_PLAIN and KIND_SILU_TABLE are the GEMM-input paths: int4 codes plus the s8 operand,
+// with no pre-op or with SwiGLU through the table.  KIND_GENERAL reads mode, bits and the
+// operand pointer at run time (SwiGLU evaluated directly, attention gate, RMSNorm).
+enum { KIND_PLAIN = 0, KIND_SILU_TABLE = 1, KIND_GENERAL = 2 };
+
+// Row-independent loads of one row's CH groups into registers (x, and the SwiGLU up /
+// attention q-gate / norm weight operand), zero where the group or row does not exist.
+template <int CH, bool AUX>
+CQ_DEV void fetch_groups(const PrepareArgs &p, int64_t row, bool ok, int wt, int lane, int ngroups,
+                         uint4 (&rx)[CH], uint4 (&ra)[CH]) {
 #pragma unroll
   for (int j = 0; j < CH; ++j) {
     const int g = wt + j * p.team_warps;
-    const bool active = row_ok && g < ngroups;
-    const int col0 = g * 256 + lane * 8;
-    uint4 raw = make_uint4(0, 0, 0, 0);
-    if (active) raw = *reinterpret_cast<const uint4 *>(xr + col0);
-    const uint16_t *h = reinterpret_cast<const uint16_t *>(&raw);
+    rx[j] = make_uint4(0, 0, 0, 0);
+    ra[j] = make_uint4(0, 0, 0, 0);
+    if (ok && g < ngroups) {
+      const int col0 = g * 256 + lane * 8;
+      rx[j] = *reinterpret_cast<const uint4 *>(p.x + row * p.x_ld + col0);
+      if (!AUX) {
+      } else if (p.mode == MODE_SWIGLU)
+        ra[j] = *reinterpret_cast<const uint4 *>(p.aux + row * p.aux_ld + col0);
+      else if (p.mode == MODE_ATTN_GATE)
+        ra[j] = *reinterpret_cast<const uint4 *>(p.aux + row * p.aux_ld + g * 512 + 256 + lane * 8);
+      else if (p.mode != MODE_PLAIN)
+        ra[j] = *reinterpret_cast<const uint4 *>(p.aux + col0);
+    }
+  }
+}
+
+// 16-byte global -> shared copy that holds no register while in flight (cp.async, L2 only);
+// a zero source size writes zeros without reading global memory.
+CQ_DEV void cp_async16(uint32_t dst, const void *src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+CQ_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CQ_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Load pipeline of a kernel instance: 0 = loads at the top of each iteration, 1 = one
+// iteration prefetched in registers, >= 2 = that many cp.async stages per thread (each
+// thread stages and later reads only its own 16-byte chunks, so the stages need no
+// barrier).  A stage is refilled as soon as its data is in registers, so all STG stages
+// are in flight while a row is rotated: about 96-128 KB per SM.
+constexpr int stages_for(int ch, int kind) {
+  return kind == KIND_PLAIN ? (ch <= 4 ? 4 : 2)
+         : kind == KIND_SILU_TABLE ? (ch == 1 ? 4 : ch == 2 ? 3 : ch == 3 ? 2 : ch == 4 ? 1 : 0)
+                                   : (ch <= 4 ? 1 : 0);
+}
+constexpr int operands_for(int kind) { return kind == KIND_PLAIN ? 1 : 2; }
+constexpr int min_blocks_for(int ch, int kind) { return kind == KIND_PLAIN && ch <= 2 ? 2 : 1; }
+
+// Issues the cp.async copies of one row's CH groups (x and, for SwiGLU, up) into a stage.
+template <int CH, int KIND>
+CQ_DEV void stage_groups(const PrepareArgs &p, uint32_t stage_base, int64_t row, bool ok, int wt, int lane,
+                         int ngroups) {
+  constexpr int NOP = operands_for(KIND);
+  const uint16_t *xr = p.x + row * p.x_ld + lane * 8;
+  const uint16_t *ar = p.aux + row * p.aux_ld + lane * 8;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[j][i] = bf16_to_f32(h[i]);
-    if (active && p.mode != MODE_PLAIN) {
-      if (p.mode == MODE_SWIGLU) {
-        uint4 uraw = *reinterpret_cast<const uint4 *>(p.aux + row * p.aux_ld + col0);
-        const uint16_t *u = reinterpret_cast<const uint16_t *>(&uraw);
+  for (int j = 0; j < CH; ++j) {
+    const int g = wt + j * p.team_warps;
+    const bool valid = ok && g < ngroups;
+    const uint32_t slot = stage_base + (uint32_t)(j * NOP) * blockDim.x * 16 + threadIdx.x * 16;
+    cp_async16(slot, valid ? (const void *)(xr + g * 256) : (const void *)p.x, valid);
+    if (NOP == 2) cp_async16(slot + blockDim.x * 16, valid ? (const void *)(ar + g * 256) : (const void *)p.x, valid);
+  }
+}
+
+// Persistent packing kernel.  A team of team_warps warps owns one row, each warp CH
+// Hadamard groups of it; rows_per_block teams per CTA; the CTA strides over row blocks.
+//
+// Per iteration: [RMSNorm partials -> barrier] -> pre-op -> Hadamard -> warp absmax ->
+// barrier -> row scale -> codes.  The per-warp maxima and norm partials are double
+// buffered by iteration parity, so one barrier per phase is enough.
+template <int CH, int KIND>
+__global__ void __launch_bounds__(512, min_blocks_for(CH, KIND)) prepare_kernel(PrepareArgs p) {
+  constexpr bool FAST = KIND != KIND_GENERAL;
+  constexpr bool TAB = KIND == KIND_SILU_TABLE;
+  constexpr int STG = stages_for(CH, KIND);
+  constexpr bool PF = STG == 1;
+  constexpr int NOP = operands_for(KIND);
+  extern __shared__ __align__(16) uint8_t smem[];
+  const uint16_t *tab = reinterpret_cast<const uint16_t *>(smem);
+  float *red = reinterpret_cast<float *>(smem + (TAB ? kSiluEntries * 2 : 0));  // [2][slots] maxima
+  const int tw = p.team_warps, rpb = p.rows_per_block;
+  const int slots = rpb * tw;
+  float *wsum = red + 2 * slots;                                                 // [2][slots] norm partials
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int team = warp / tw, wt = warp % tw;
+  const int tid_team = wt * 32 + lane;
+  const int ngroups = p.width >> 8;
+  const int bits = FAST ? 4 : p.bits;
+  const bool has_op = FAST || p.op8 != nullptr;
+  const int words = FAST ? p.stride >> 3 : p.stride / (32 / bits);
+  const int code_words = FAST ? p.width >> 3 : p.width / (32 / bits);
+  const bool norm = KIND == KIND_GENERAL && (p.mode == MODE_NORM || p.mode == MODE_NORM_STORE);
+  const int64_t nblk = (p.rows + rpb - 1) / rpb;
+  const float qmax = bits == 8 ? 127.0f : 7.0f;
+  // this lane's word inside its 32-code operand block (low-nibble half; high half +16 B)
+  const int lane_op = (lane >> 2) * 32 + (lane & 3) * 4;
+  // cp.async stages follow the maxima and norm partials: [STG][CH][NOP][threads] x 16 B
+  const uint32_t stage0 = smem_u32(wsum + 2 * slots);
+  const uint32_t stage_bytes = (uint32_t)(CH * NOP) * blockDim.x * 16;
+
+  uint4 rx[CH], ra[CH];
+  int64_t blk = blockIdx.x;
+  if (PF) fetch_groups<CH, KIND != KIND_PLAIN>(p, blk * rpb + team, blk * rpb + team < p.rows, wt, lane, ngroups, rx, ra);
+  if (STG >= 2) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float g0 = v[j][i];
-          float act = __fdiv_rn(g0, __fadd_rn(1.0f, exp_cw(-g0)));
-          v[j][i] = bf16r(__fmul_rn(bf16r(act), bf16_to_f32(u[i])));
+    for (int st = 0; st < STG; ++st) {
+      const int64_t b = blk + (int64_t)st * gridDim.x;
+      stage_groups<CH, KIND>(p, stage0 + st * stage_bytes, b * rpb + team, b < nblk && b * rpb + team < p.rows, wt,
+                             lane, ngroups);
+      cp_async_commit();
+    }
+  }
+  if (TAB) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(g_silu_bf16);
+    uint4 *dst = reinterpret_cast<uint4 *>(smem);
+    for (int i = threadIdx.x; i < kSiluEntries * 2 / 16; i += blockDim.x) dst[i] = src[i];
+    __syncthreads();
+  }
+  int par = 0, st = 0;
+  for (; blk < nblk; blk += gridDim.x, par ^= 1) {
+    const int64_t row = blk * rpb + team;
+    const bool row_ok = row < p.rows;
+    if (STG == 0) fetch_groups<CH, KIND != KIND_PLAIN>(p, row, row_ok, wt, lane, ngroups, rx, ra);
+    if (STG >= 2) {
+      cp_async_wait<STG - 1>();  // this block's copies (all but the STG-1 newest groups)
+      const uint32_t base = stage0 + st * stage_bytes + threadIdx.x * 16;
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        rx[j] = lds_v4(base + (uint32_t)(j * NOP) * blockDim.x * 16);
+        if (NOP == 2) ra[j] = lds_v4(base + (uint32_t)(j * NOP + 1) * blockDim.x * 16);
+      }
+    }
+
+    // RMSNorm: 256 strided partial sums -> warp butterflies -> the 8 warp totals in order.
+    float norm_inv = 1.0f;
+    if (norm) {
+      const uint16_t *xr = p.x + (row_ok ? row : 0) * p.x_ld;
+      float s = 0.0f;
+      for (int j = tid_team; j < p.width; j += 256) {
+        float v = bf16_to_f32(xr[j]);
+        s = __fmaf_rn(v, v, s);
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+      float *ws = wsum + par * slots + team * tw;
+      if (lane == 0) ws[wt] = s;
+      __syncthreads();
+      float total = ws[0];
+      for (int w = 1; w < 8; ++w) total = __fadd_rn(total, ws[w]);
+      float var = __fdiv_rn(total, (float)p.width);
+      norm_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-6f)));
+    }
+
+    float v[CH][8];
+#pragma unroll
+    for (int j = 0; j < CH; ++j) {
+      const uint16_t *h = reinterpret_cast<const uint16_t *>(&rx[j]);
+      const uint16_t *a = reinterpret_cast<const uint16_t *>(&ra[j]);
+      if (TAB) {
+        const uint32_t *gw = reinterpret_cast<const uint32_t *>(&rx[j]);
+        const uint32_t *uw = reinterpret_cast<const uint32_t *>(&ra[j]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float lo = __fmul_rn(bf16_to_f32(tab[gw[k] & 0xffffu]), __uint_as_float(uw[k] << 16));
+          float hi = __fmul_rn(bf16_to_f32(tab[gw[k] >> 16]), __uint_as_float(uw[k] & 0xffff0000u));
+          bf16r_pair(lo, hi);
+          v[j][2 * k] = lo;
+          v[j][2 * k + 1] = hi;
         }
-      } else if (p.mode == MODE_ATTN_GATE) {
-        const int head = col0 >> 8, within = col0 & 255;
-        uint4 qraw = *reinterpret_cast<const uint4 *>(p.aux + row * p.aux_ld + head * 512 + 256 + within);
-        const uint16_t *q = reinterpret_cast<const uint16_t *>(&qraw);
+        continue;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[j][i] = bf16_to_f32(h[i]);
+      if (KIND == KIND_PLAIN) continue;
+      const int g = wt + j * tw;
+      const bool active = row_ok && g < ngroups;
+      if (active && p.mode == MODE_SWIGLU) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] = bf16r(__fmul_rn(bf16_to_f32(silu_bf16(h[i])), bf16_to_f32(a[i])));
+      } else if (active && p.mode == MODE_ATTN_GATE) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          float sg = bf16r(__fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cw(-bf16_to_f32(q[i])))));
+          float sg = bf16r(__fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cw(-bf16_to_f32(a[i])))));
           v[j][i] = bf16r(__fmul_rn(v[j][i], sg));
         }
-      } else {
-        uint4 wraw = *reinterpret_cast<const uint4 *>(p.aux + col0);
-        const uint16_t *w = reinterpret_cast<const uint16_t *>(&wraw);
-        uint16_t nh[8];
+      } else if (active && norm) {
+        uint4 nh4;
+        uint16_t *nh = reinterpret_cast<uint16_t *>(&nh4);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          float wf = __fadd_rn(bf16_to_f32(w[i]), 1.0f);
+          float wf = __fadd_rn(bf16_to_f32(a[i]), 1.0f);
           float nn = __fmul_rn(__fsub_rn(v[j][i], 0.0f), norm_inv);
           nh[i] = f32_to_bf16(__fmaf_rn(nn, wf, 0.0f));
           v[j][i] = bf16_to_f32(nh[i]);
         }
         if (p.mode == MODE_NORM_STORE)
-          *reinterpret_cast<uint4 *>(p.norm_out + row * p.norm_ld + col0) = *reinterpret_cast<uint4 *>(nh);
+          *reinterpret_cast<uint4 *>(p.norm_out + row * p.norm_ld + g * 256 + lane * 8) = nh4;
       }
     }
-    hadamard256_lane(v[j], lane);
-    if (active) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float a = fabsf(v[j][i]);
-        m = maxnum(m, a < __int_as_float(0x7f800000) ? a : __int_as_float(0x7f800000));
-      }
+    // the stage is in registers now: refill it with the block STG iterations ahead
+    if (STG >= 2) {
+      const int64_t b = blk + (int64_t)STG * gridDim.x;
+      stage_groups<CH, KIND>(p, stage0 + st * stage_bytes, b * rpb + team, b < nblk && b * rpb + team < p.rows, wt,
+                             lane, ngroups);
+      cp_async_commit();
+      st = st + 1 == STG ? 0 : st + 1;
     }
-  }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) m = maxnum(m, __shfl_xor_sync(0xffffffffu, m, off));
-  if (lane == 0) red[team * p.team_warps + wt] = m;
-  __syncthreads();
-  float rmax = 0.0f;
-  for (int w = 0; w < p.team_warps; ++w) rmax = maxnum(rmax, red[team * p.team_warps + w]);
-  if (!row_ok) return;
+    if (PF) {
+      const int64_t nrow = (blk + gridDim.x) * rpb + team;
+      fetch_groups<CH, KIND != KIND_PLAIN>(p, nrow, blk + gridDim.x < nblk && nrow < p.rows, wt, lane, ngroups, rx, ra);
+    }
 
-  const float qmax = bits == 8 ? 127.0f : 7.0f;
-  const float scale = __fdiv_rn(maxnum(__fmul_rn(rmax, 0.0625f), 1e-30f), qmax);
-  const bool valid = scale < __int_as_float(0x7f800000);
-  const float inv = __fdiv_rn(0.0625f, scale);
-  uint32_t *orow = p.out + row * words;
+    // Rotation and row absmax; absent groups and rows hold zeros.  NaN propagates and
+    // becomes +inf, like the reference's clamp of non-finite magnitudes.
+    float m = 0.0f;
 #pragma unroll
-  for (int j = 0; j < CH; ++j) {
-    const int g = wt + j * p.team_warps;
-    if (g >= ngroups) continue;
-    const int col0 = g * 256 + lane * 8;
-    int code[8];
+    for (int j = 0; j < CH; ++j) {
+      hadamard256_lane(v[j]);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float sc = valid ? __fmul_rn(v[j][i], inv) : 0.0f;
-      float c = minnum(maxnum(rintf(sc), -qmax), qmax);
-      code[i] = (int)c;
+      for (int i = 0; i < 8; i += 2) m = absmax3_nan(m, v[j][i], v[j][i + 1]);
     }
-    if (bits == 4) {
-      uint32_t w = 0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w |= ((uint32_t)code[i] & 0xFu) << (4 * i);
-      orow[col0 >> 3] = w;
-      if (p.op8) {
-        // word q = col0/8 is word (q & 3) of 32-code group q >> 2
-        uint8_t *grp = p.op8 + row * p.op_ld + (int64_t)(col0 >> 5) * 32;
-        const int i4 = (col0 >> 3) & 3;
-        *reinterpret_cast<uint32_t *>(grp + 4 * i4) = nib_lo16(w);
-        *reinterpret_cast<uint32_t *>(grp + 16 + 4 * i4) = nib_hi16(w);
+    for (int off = 16; off >= 1; off >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (m != m) m = __int_as_float(0x7f800000);
+    float *rs = red + par * slots + team * tw;
+    if (lane == 0) rs[wt] = m;
+    __syncthreads();
+    // the team's maxima, one per lane, reduced across the lanes (tw <= 16)
+    float rmax = lane < tw ? rs[lane] : 0.0f;
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) rmax = maxnum(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+    rmax = __shfl_sync(0xffffffffu, rmax, 0);
+    if (!row_ok) continue;
+
+    const float scale = __fdiv_rn(maxnum(__fmul_rn(rmax, 0.0625f), 1e-30f), qmax);
+    const float inv = __fdiv_rn(0.0625f, scale);
+    uint32_t *orow = p.out + row * words;
+    uint8_t *oprow = has_op ? p.op8 + row * p.op_ld + lane_op : nullptr;
+    if (scale < __int_as_float(0x7f800000)) {
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        const int g = wt + j * tw;
+        if (g >= ngroups) continue;
+        int c[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) c[i] = rint_s32(__fmul_rn(v[j][i], inv));
+        if (bits == 4) {
+          const uint32_t w = pack_s4(c[1], c[0], pack_s4(c[3], c[2], pack_s4(c[5], c[4], pack_s4(c[7], c[6], 0u))));
+          orow[g * 32 + lane] = w;
+          if (has_op) {
+            // word g*32 + lane is word (lane & 3) of its 32-code group: the s8 operand holds
+            // 16 * code, low nibbles of the group's 4 words first, then high nibbles
+            *reinterpret_cast<uint32_t *>(oprow + g * 256) = nib_lo16(w);
+            *reinterpret_cast<uint32_t *>(oprow + g * 256 + 16) = nib_hi16(w);
+          }
+        } else {
+          *reinterpret_cast<uint2 *>(orow + g * 64 + lane * 2) =
+              make_uint2(pack_s8(c[1], c[0], pack_s8(c[3], c[2], 0u)), pack_s8(c[5], c[4], pack_s8(c[7], c[6], 0u)));
+        }
       }
     } else {
-      uint32_t w0 = 0, w1 = 0;
+      // a non-finite row: zero codes, infinite scale
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        w0 |= ((uint32_t)code[i] & 0xFFu) << (8 * i);
-        w1 |= ((uint32_t)code[i + 4] & 0xFFu) << (8 * i);
+      for (int j = 0; j < CH; ++j) {
+        const int g = wt + j * tw;
+        if (g >= ngroups) continue;
+        if (bits == 4) {
+          orow[g * 32 + lane] = 0u;
+          if (has_op) {
+            *reinterpret_cast<uint32_t *>(oprow + g * 256) = 0u;
+            *reinterpret_cast<uint32_t *>(oprow + g * 256 + 16) = 0u;
+          }
+        } else {
+          *reinterpret_cast<uint2 *>(orow + g * 64 + lane * 2) = make_uint2(0u, 0u);
+        }
       }
-      *reinterpret_cast<uint2 *>(orow + (col0 >> 2)) = make_uint2(w0, w1);
     }
+    // Stride padding words are zeroed; the scale follows all code rows.
+    for (int w = code_words + tid_team; w < words; w += tw * 32) orow[w] = 0u;
+    if (tid_team == 0) reinterpret_cast<float *>(p.out + p.rows * words)[row] = scale;
   }
-  // Stride padding words are zeroed; the scale follows all code rows.
-  const int tid_in_team = wt * 32 + lane;
-  for (int w = p.width / P + tid_in_team; w < words; w += p.team_warps * 32) orow[w] = 0u;
-  if (tid_in_team == 0) reinterpret_cast<float *>(p.out + p.rows * words)[row] = scale;
+  if (STG >= 2) cp_async_wait<0>();
 }
+
+namespace {
+// Per-device launch facts of one kernel instance: resident CTAs per SM for a block size.
+// The dynamic shared-memory limit is one attribute per kernel, so it is raised once per
+// device to what the instance can need at its largest block (512 threads, 16 team slots).
+constexpr int kMaxDevices = 64;
+template <int CH, int KIND>
+size_t max_smem_bytes() {
+  constexpr int STG = stages_for(CH, KIND);
+  return (KIND == KIND_SILU_TABLE ? kSiluEntries * 2 : 0) + sizeof(float) * 4 * 16 +
+         (STG >= 2 ? (size_t)STG * CH * operands_for(KIND) * 512 * 16 : 0);
+}
+
+template <int CH, int KIND>
+int resident_ctas(int threads, size_t smem) {
+  static int cache[kMaxDevices][17];
+  static bool attr[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int warps = threads / 32 > 16 ? 16 : threads / 32;
+  if (dev < 0 || dev >= kMaxDevices) return 1;
+  if (!attr[dev]) {
+    const size_t most = max_smem_bytes<CH, KIND>();
+    if (most > 48 * 1024)
+      cudaFuncSetAttribute(prepare_kernel<CH, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most);
+    attr[dev] = true;
+  }
+  if (!cache[dev][warps]) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, prepare_kernel<CH, KIND>, threads, smem) != cudaSuccess ||
+        n <= 0)
+      n = 1;
+    cache[dev][warps] = n;
+  }
+  return cache[dev][warps];
+}
+
+template <int CH, int KIND>
+void launch_instance(const PrepareArgs &a, int threads, size_t smem0, int64_t nblk, cudaStream_t stream) {
+  constexpr int STG = stages_for(CH, KIND);
+  const size_t smem = smem0 + (STG >= 2 ? (size_t)STG * CH * operands_for(KIND) * threads * 16 : 0);
+  const int per_sm = resident_ctas<CH, KIND>(threads, smem);
+  int64_t grid = (int64_t)device_sms() * per_sm;
+  if (grid > nblk) grid = nblk;
+  prepare_kernel<CH, KIND><<<(unsigned)grid, threads, smem, stream>>>(a);
+}
+
+template <int KIND>
+bool launch_kind(int ch, const PrepareArgs &a, int threads, size_t smem, int64_t nblk, cudaStream_t stream) {
+  switch (ch) {
+    case 1: launch_instance<1, KIND>(a, threads, smem, nblk, stream); return true;
+    case 2: launch_instance<2, KIND>(a, threads, smem, nblk, stream); return true;
+    case 3: launch_instance<3, KIND>(a, threads, smem, nblk, stream); return true;
+    case 4: launch_instance<4, KIND>(a, threads, smem, nblk, stream); return true;
+    case 5: launch_instance<5, KIND>(a, threads, smem, nblk, stream); return true;
+    case 6: launch_instance<6, KIND>(a, threads, smem, nblk, stream); return true;
+    case 7: launch_instance<7, KIND>(a, threads, smem, nblk, stream); return true;
+    case 8: launch_instance<8, KIND>(a, threads, smem, nblk, stream); return true;
+  }
+  return false;
+}
+}  // namespace
 
 int launch_prepare(const PrepareArgs &a0, cudaStream_t stream) {
   PrepareArgs a = a0;
   const int ngroups = a.width >> 8;
   const bool norm = a.mode == MODE_NORM || a.mode == MODE_NORM_STORE;
-  int tw, rpb;
+  const bool gemm_input = a.bits == 4 && a.op8 != nullptr;
+  // The table pays for its 128 KB shared-memory fill once a launch has about a full
+  // wave of groups to process; small launches evaluate the activation directly.
+  const bool tab = gemm_input && a.mode == MODE_SWIGLU && a.rows * (int64_t)ngroups >= 2048;
+  const int kind = gemm_input && a.mode == MODE_PLAIN ? KIND_PLAIN : tab ? KIND_SILU_TABLE : KIND_GENERAL;
+  int tw, ch;
   if (norm) {
-    tw = 8;
-    rpb = 1;
-  } else if (ngroups >= 16) {
-    tw = 16;
-    rpb = 1;
-  } else if (ngroups >= 8) {
-    tw = 8;
-    rpb = 1;
+    tw = 8;  // the reference's 256-thread reduction order
+    ch = (ngroups + 7) / 8;
   } else {
-    tw = ngroups;
-    rpb = 8 / ngroups;
+    // plain rows: 4 groups per lane amortise the per-row work; table rows: up to 16
+    // warps per row (one CTA per SM); otherwise 2 groups per lane
+    ch = kind == KIND_PLAIN ? (ngroups < 4 ? ngroups : 4) : tab ? (ngroups + 15) / 16 : (ngroups >= 2 ? 2 : 1);
+    if ((ngroups + ch - 1) / ch > 16) ch = (ngroups + 15) / 16;
+    tw = (ngroups + ch - 1) / ch;
   }
-  const int ch = (ngroups + tw - 1) / tw;
+  if (ch < 1 || ch > 8 || tw < 1) return report_error(CLEFQ_ERR_SHAPE, "prepare: row width above the supported maximum");
+  const int rpb = 16 / tw > 0 ? 16 / tw : 1;
   a.team_warps = tw;
   a.rows_per_block = rpb;
   const int threads = tw * 32 * rpb;
-  const int64_t blocks = (a.rows + rpb - 1) / rpb;
-  const size_t smem = sizeof(float) * (size_t)(tw * rpb + 8);
-  if (blocks == 0) return 0;
-  if (blocks > 0x7fffffffLL) return CLEFQ_ERR_SHAPE;
-  switch (ch) {
-#define CQ_CASE(N) \
-  case N: prepare_kernel<N><<<(unsigned)blocks, threads, smem, stream>>>(a); break;
-    CQ_CASE(1) CQ_CASE(2) CQ_CASE(3) CQ_CASE(4) CQ_CASE(5) CQ_CASE(6) CQ_CASE(7) CQ_CASE(8)
-#undef CQ_CASE
-    default:
-      return CLEFQ_ERR_SHAPE;
-  }
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  const int64_t nblk = (a.rows + rpb - 1) / rpb;
+  const size_t smem = (tab ? kSiluEntries * 2 : 0) + sizeof(float) * 4 * (size_t)(tw * rpb);
+  if (nblk == 0) return 0;
+  bool ok = kind == KIND_PLAIN        ? launch_kind<KIND_PLAIN>(ch, a, threads, smem, nblk, stream)
+            : kind == KIND_SILU_TABLE ? launch_kind<KIND_SILU_TABLE>(ch, a, threads, smem, nblk, stream)
+                                      : launch_kind<KIND_GENERAL>(ch, a, threads, smem, nblk, stream);
+  if (!ok) return report_error(CLEFQ_ERR_SHAPE, "prepare: no kernel for this row width");
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : report_error(CLEFQ_ERR_CUDA, cudaGetErrorString(e));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -255,9 +522,7 @@ __global__ void swiglu_kernel(const uint16_t *__restrict__ g, const uint16_t *__
     uint16_t *oh = reinterpret_cast<uint16_t *>(&o);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      float a = bf16_to_f32(gh[k]);
-      float act = __fdiv_rn(a, __fadd_rn(1.0f, exp_cw(-a)));
-      oh[k] = f32_to_bf16(__fmul_rn(bf16r(act), bf16_to_f32(uh[k])));
+      oh[k] = f32_to_bf16(__fmul_rn(bf16_to_f32(silu_bf16(gh[k])), bf16_to_f32(uh[k])));
     }
     reinterpret_cast<uint4 *>(out)[i] = o;
   }
@@ -265,9 +530,7 @@ __global__ void swiglu_kernel(const uint16_t *__restrict__ g, const uint16_t *__
 __global__ void swiglu_tail_kernel(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t start, int64_t n) {
   int64_t i = start + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i < n) {
-    float a = bf16_to_f32(g[i]);
-    float act = __fdiv_rn(a, __fadd_rn(1.0f, exp_cw(-a)));
-    out[i] = f32_to_bf16(__fmul_rn(bf16r(act), bf16_to_f32(u[i])));
+    out[i] = f32_to_bf16(__fmul_rn(bf16_to_f32(silu_bf16(g[i])), bf16_to_f32(u[i])));
   }
 }
 

@@ -109,6 +109,32 @@ def test_fused_swiglu_packing(cq, rows, width, bits):
     assert torch.equal(sep.storage, fused.storage)
 
 
+@pytest.mark.parametrize("rows,width", [(701, 768), (257, 1280), (300, 4096), (1201, 12288),
+                                        (150, 20480), (70, 32768)])
+@pytest.mark.parametrize("bits", [4, 8])
+def test_swiglu_table_packing(cq, rows, width, bits):
+    """Launches with at least a wave of groups take the SiLU-table kernel; every row count,
+    group split and persistent-loop length must still equal the oracle bit for bit."""
+    rng = np.random.default_rng(rows * 7 + width)
+    g = _gate_like(rng, rows, width)
+    u = bf16_normal(rng, (rows, width), 2.0)
+    stride = width + 512 // bits
+    fused = _dev_prepared(cq, g, bits, stride, cq.PREP_SWIGLU, u)
+    storage, _, _, _ = o.prepare(g, bits, stride, o.SWIGLU, u)
+    assert np.array_equal(fused.storage.cpu().numpy().view(np.uint32), storage)
+
+
+@pytest.mark.parametrize("rows,width", [(3000, 4096), (4001, 512), (999, 1792)])
+def test_plain_packing_many_row_blocks(cq, rows, width):
+    """Plain packing over more row blocks than resident CTAs (prefetch across iterations)."""
+    rng = np.random.default_rng(rows)
+    x = bf16_normal(rng, (rows, width), 1.5)
+    stride = o.stride_for(width)
+    p = _dev_prepared(cq, x, 4, stride, cq.PREP_PLAIN, None)
+    storage, _, _, _ = o.prepare(x, 4, stride, o.PLAIN, None)
+    assert np.array_equal(p.storage.cpu().numpy().view(np.uint32), storage)
+
+
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("rows", [1, 158])
 def test_attention_gate_packing(cq, bits, rows):
