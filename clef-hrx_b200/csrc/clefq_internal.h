@@ -24,6 +24,7 @@ struct PrepareArgs {
   int64_t norm_ld;
   int team_warps;       // warps per row (set by launch_prepare)
   int rows_per_block;
+  int stages;           // cp.async stages per thread (GEMM-input packing kernel)
 };
 int launch_prepare(const PrepareArgs &a, cudaStream_t stream);
 int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);

@@ -32,9 +32,10 @@ enum { MODE_PLAIN = 0, MODE_SWIGLU = 1, MODE_ATTN_GATE = 2, MODE_NORM = 3, MODE_
 // which are the reference's rounded results because x - y = -(y - x) and s + (-t) = s - t
 // exactly under round-to-nearest-even.  Only the sign of an exact zero can differ, and no
 // code or row scale depends on it.
-CQ_DEV void radix4_lanes(float (&v)[8], int xmask, int ymask) {
+template <int N>
+CQ_DEV void radix4_lanes(float (&v)[N], int xmask, int ymask) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < N; ++i) {
     const float own = v[i];
     const float peer = __shfl_xor_sync(0xffffffffu, own, xmask);
     const float s = __fadd_rn(own, peer);
@@ -410,6 +411,195 @@ __global__ void __launch_bounds__(512, min_blocks_for(CH, KIND)) prepare_kernel(
   if (STG >= 2) cp_async_wait<0>();
 }
 
+// ---------------------------------------------------------------------------------------
+// GEMM-input packing (int4 codes + s8 operand, no pre-op or SwiGLU through the table).
+// Eight lanes share a group and a lane holds 32 of its elements: element
+// e = 64 k + 8 r + t (r = lane & 7, k = 0..3, t = 0..7) sits in v[8 k + t], so a warp
+// covers four groups per slot and every 16-byte load of the eight lanes is one contiguous
+// 128-byte line.  Hadamard strides 1 and 64 run inside the lane, stride 4 pairs lane r
+// with r ^ 1 (one shuffle per two elements), stride 16 spans lanes r, r ^ 2, r ^ 4, r ^ 6:
+// 9 adds and 2.5 shuffles per element.  For each k a lane's eight codes are one code word.
+// ---------------------------------------------------------------------------------------
+CQ_DEV void radix4_in_lane(float &a, float &b, float &c, float &d) {
+  const float s01 = __fadd_rn(a, b), s23 = __fadd_rn(c, d), d01 = __fsub_rn(a, b), d23 = __fsub_rn(c, d);
+  a = __fadd_rn(s01, d23);
+  b = __fsub_rn(s01, d23);
+  c = __fadd_rn(d01, s23);
+  d = __fsub_rn(s23, d01);
+}
+
+CQ_DEV void hadamard256_x32(float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 32; q += 4) radix4_in_lane(v[q], v[q + 1], v[q + 2], v[q + 3]);  // stride 1
+  // stride 4: (a, b) = (v[8k+u], v[8k+u+4]) of the even lane, (c, d) of the odd lane
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float x = v[8 * k + u], y = v[8 * k + u + 4];
+      const float s = __fadd_rn(x, y), d = __fsub_rn(x, y);
+      const float p2 = __shfl_xor_sync(0xffffffffu, d, 1);
+      v[8 * k + u] = __fadd_rn(s, p2);
+      v[8 * k + u + 4] = __fsub_rn(s, p2);
+    }
+  }
+  radix4_lanes(v, 2, 4);  // stride 16
+#pragma unroll
+  for (int t = 0; t < 8; ++t) radix4_in_lane(v[t], v[8 + t], v[16 + t], v[24 + t]);  // stride 64
+}
+
+CQ_DEV void cp_async_wait_dyn(int n) {
+  if (n <= 0) cp_async_wait<0>();
+  else if (n == 1) cp_async_wait<1>();
+  else if (n == 2) cp_async_wait<2>();
+  else cp_async_wait<3>();
+}
+
+constexpr int kPackRedBytes = 4 * 16 * 4;  // [2][16] warp maxima, padded
+
+// NS slots (of four groups) per warp, team_warps warps per row, rows_per_block rows per
+// CTA; p.stages cp.async stages per thread of NS x NOP x 64 bytes each.
+template <int NS, bool TAB>
+__global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
+  constexpr int NOP = TAB ? 2 : 1;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const uint16_t *tab = reinterpret_cast<const uint16_t *>(smem);
+  float *red = reinterpret_cast<float *>(smem + (TAB ? kSiluEntries * 2 : 0));  // [2][slots]
+  const int tw = p.team_warps, rpb = p.rows_per_block, slots = tw * rpb;
+  const int nstg = p.stages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int team = warp / tw, wt = warp % tw;
+  const int tid_team = wt * 32 + lane;
+  const int ngroups = p.width >> 8;
+  const int words = p.stride >> 3;
+  const int code_words = p.width >> 3;
+  const int q = lane >> 3, r = lane & 7;
+  const int64_t nblk = (p.rows + rpb - 1) / rpb;
+  const uint32_t stage0 = smem_u32(smem + (TAB ? kSiluEntries * 2 : 0) + kPackRedBytes);
+  const uint32_t chunk = blockDim.x * 16;                    // one 16-byte chunk per thread
+  const uint32_t stage_bytes = (uint32_t)(NS * NOP * 4) * chunk;
+  int gidx[NS];                                              // this lane's group per slot
+#pragma unroll
+  for (int sl = 0; sl < NS; ++sl) gidx[sl] = (sl * tw + wt) * 4 + q;
+
+  auto issue = [&](int64_t b, int stg) {
+    const int64_t row = b * rpb + team;
+    const bool ok = b < nblk && row < p.rows;
+    const uint32_t base = stage0 + stg * stage_bytes + threadIdx.x * 16;
+#pragma unroll
+    for (int sl = 0; sl < NS; ++sl) {
+      const bool valid = ok && gidx[sl] < ngroups;
+      const int64_t off = row * p.x_ld + gidx[sl] * 256 + r * 8;
+      const int64_t aoff = row * p.aux_ld + gidx[sl] * 256 + r * 8;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        cp_async16(base + ((sl * NOP) * 4 + k) * chunk, valid ? (const void *)(p.x + off + k * 64) : (const void *)p.x,
+                   valid);
+        if (NOP == 2)
+          cp_async16(base + ((sl * NOP + 1) * 4 + k) * chunk,
+                     valid ? (const void *)(p.aux + aoff + k * 64) : (const void *)p.x, valid);
+      }
+    }
+    cp_async_commit();
+  };
+
+  int64_t blk = blockIdx.x;
+  for (int st = 0; st < nstg; ++st) issue(blk + (int64_t)st * gridDim.x, st);
+  if (TAB) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(g_silu_bf16);
+    uint4 *dst = reinterpret_cast<uint4 *>(smem);
+    for (int i = threadIdx.x; i < kSiluEntries * 2 / 16; i += blockDim.x) dst[i] = src[i];
+    __syncthreads();
+  }
+  int par = 0, st = 0;
+  for (; blk < nblk; blk += gridDim.x, par ^= 1) {
+    const int64_t row = blk * rpb + team;
+    const bool row_ok = row < p.rows;
+    cp_async_wait_dyn(nstg - 1);  // this block's copies (all but the nstg-1 newest groups)
+    const uint32_t base = stage0 + st * stage_bytes + threadIdx.x * 16;
+    float v[NS][32];
+#pragma unroll
+    for (int sl = 0; sl < NS; ++sl) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint4 gx = lds_v4(base + ((sl * NOP) * 4 + k) * chunk);
+        const uint32_t gw[4] = {gx.x, gx.y, gx.z, gx.w};
+        if (TAB) {
+          const uint4 ux = lds_v4(base + ((sl * NOP + 1) * 4 + k) * chunk);
+          const uint32_t uw[4] = {ux.x, ux.y, ux.z, ux.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            float lo = __fmul_rn(bf16_to_f32(tab[gw[t] & 0xffffu]), __uint_as_float(uw[t] << 16));
+            float hi = __fmul_rn(bf16_to_f32(tab[gw[t] >> 16]), __uint_as_float(uw[t] & 0xffff0000u));
+            bf16r_pair(lo, hi);
+            v[sl][8 * k + 2 * t] = lo;
+            v[sl][8 * k + 2 * t + 1] = hi;
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            v[sl][8 * k + 2 * t] = __uint_as_float(gw[t] << 16);
+            v[sl][8 * k + 2 * t + 1] = __uint_as_float(gw[t] & 0xffff0000u);
+          }
+        }
+      }
+    }
+    // the stage is in registers now: refill it with the block nstg iterations ahead
+    issue(blk + (int64_t)nstg * gridDim.x, st);
+    st = st + 1 == nstg ? 0 : st + 1;
+
+    float m = 0.0f;
+#pragma unroll
+    for (int sl = 0; sl < NS; ++sl) {
+      hadamard256_x32(v[sl]);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) m = absmax3_nan(m, v[sl][i], v[sl][i + 1]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (m != m) m = __int_as_float(0x7f800000);
+    float *rs = red + par * slots + team * tw;
+    if (lane == 0) rs[wt] = m;
+    __syncthreads();
+    float rmax = lane < tw ? rs[lane] : 0.0f;
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) rmax = maxnum(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+    rmax = __shfl_sync(0xffffffffu, rmax, 0);
+    if (!row_ok) continue;
+
+    const float scale = __fdiv_rn(maxnum(__fmul_rn(rmax, 0.0625f), 1e-30f), 7.0f);
+    const float inv = __fdiv_rn(0.0625f, scale);
+    const bool finite = scale < __int_as_float(0x7f800000);
+    uint32_t *orow = p.out + row * words;
+    uint8_t *oprow = p.op8 + row * p.op_ld;
+#pragma unroll
+    for (int sl = 0; sl < NS; ++sl) {
+      const int g = gidx[sl];
+      if (g >= ngroups) continue;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint32_t w = 0u;
+        if (finite) {
+          int c[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) c[i] = rint_s32(__fmul_rn(v[sl][8 * k + i], inv));
+          w = pack_s4(c[1], c[0], pack_s4(c[3], c[2], pack_s4(c[5], c[4], pack_s4(c[7], c[6], 0u))));
+        }
+        // code word g*32 + 8k + r is word (r & 3) of its 32-code operand block: the s8
+        // operand holds 16 * code, low nibbles of the block's 4 words first, then high
+        orow[g * 32 + 8 * k + r] = w;
+        uint8_t *op = oprow + g * 256 + k * 64 + (r >> 2) * 32 + (r & 3) * 4;
+        *reinterpret_cast<uint32_t *>(op) = nib_lo16(w);
+        *reinterpret_cast<uint32_t *>(op + 16) = nib_hi16(w);
+      }
+    }
+    // Stride padding words are zeroed; the scale follows all code rows.
+    for (int w = code_words + tid_team; w < words; w += tw * 32) orow[w] = 0u;
+    if (tid_team == 0) reinterpret_cast<float *>(p.out + p.rows * words)[row] = scale;
+  }
+  cp_async_wait<0>();
+}
+
 namespace {
 // Per-device launch facts of one kernel instance: resident CTAs per SM for a block size.
 // The dynamic shared-memory limit is one attribute per kernel, so it is raised once per
@@ -472,23 +662,70 @@ bool launch_kind(int ch, const PrepareArgs &a, int threads, size_t smem, int64_t
 }
 }  // namespace
 
+namespace {
+template <int NS, bool TAB>
+void launch_pack(const PrepareArgs &a, int threads, size_t smem, int64_t nblk, cudaStream_t stream) {
+  static bool attr[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices || !attr[dev]) {
+    // largest request of this instance: table + maxima + the stage budget
+    const int most = (TAB ? kSiluEntries * 2 : 0) + kPackRedBytes + (TAB ? 96 : 128) * 1024;
+    cudaFuncSetAttribute(pack_kernel<NS, TAB>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    if (dev >= 0 && dev < kMaxDevices) attr[dev] = true;
+  }
+  int64_t grid = device_sms();
+  if (grid > nblk) grid = nblk;
+  pack_kernel<NS, TAB><<<(unsigned)grid, threads, smem, stream>>>(a);
+}
+
+// GEMM-input packing: int4 codes with the s8 operand, 16-byte aligned rows, no pre-op or
+// SwiGLU through the table.  Returns false when the shape needs the general kernel.
+bool try_launch_pack(PrepareArgs a, bool tab, cudaStream_t stream) {
+  const int ngroups = a.width >> 8;
+  const int sg = (ngroups + 3) / 4;  // slots of four groups
+  const int ns = (sg + 15) / 16;
+  if (ns > (tab ? 1 : 2)) return false;
+  const int tw = (sg + ns - 1) / ns;
+  const int rpb = 16 / tw > 0 ? 16 / tw : 1;
+  const int threads = tw * 32 * rpb;
+  const size_t per_stage = (size_t)threads * ns * (tab ? 2 : 1) * 64;
+  int stages = (int)(((tab ? 96 : 128) * 1024) / per_stage);
+  if (stages > 4) stages = 4;
+  if (stages < 1) return false;
+  a.team_warps = tw;
+  a.rows_per_block = rpb;
+  a.stages = stages;
+  const size_t smem = (tab ? kSiluEntries * 2 : 0) + kPackRedBytes + stages * per_stage;
+  const int64_t nblk = (a.rows + rpb - 1) / rpb;
+  if (ns == 1)
+    tab ? launch_pack<1, true>(a, threads, smem, nblk, stream) : launch_pack<1, false>(a, threads, smem, nblk, stream);
+  else
+    launch_pack<2, false>(a, threads, smem, nblk, stream);
+  return true;
+}
+}  // namespace
+
 int launch_prepare(const PrepareArgs &a0, cudaStream_t stream) {
   PrepareArgs a = a0;
   const int ngroups = a.width >> 8;
   const bool norm = a.mode == MODE_NORM || a.mode == MODE_NORM_STORE;
-  const bool gemm_input = a.bits == 4 && a.op8 != nullptr;
+  if (a.rows == 0) return 0;
+  const bool gemm_input = a.bits == 4 && a.op8 != nullptr && ((uintptr_t)a.out & 15) == 0 &&
+                          (a.x_ld & 7) == 0 && (a.mode != MODE_SWIGLU || (a.aux_ld & 7) == 0);
   // The table pays for its 128 KB shared-memory fill once a launch has about a full
   // wave of groups to process; small launches evaluate the activation directly.
   const bool tab = gemm_input && a.mode == MODE_SWIGLU && a.rows * (int64_t)ngroups >= 2048;
-  const int kind = gemm_input && a.mode == MODE_PLAIN ? KIND_PLAIN : tab ? KIND_SILU_TABLE : KIND_GENERAL;
+  if (gemm_input && (a.mode == MODE_PLAIN || tab) && try_launch_pack(a, tab, stream)) {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : report_error(CLEFQ_ERR_CUDA, cudaGetErrorString(e));
+  }
   int tw, ch;
   if (norm) {
     tw = 8;  // the reference's 256-thread reduction order
     ch = (ngroups + 7) / 8;
   } else {
-    // plain rows: 4 groups per lane amortise the per-row work; table rows: up to 16
-    // warps per row (one CTA per SM); otherwise 2 groups per lane
-    ch = kind == KIND_PLAIN ? (ngroups < 4 ? ngroups : 4) : tab ? (ngroups + 15) / 16 : (ngroups >= 2 ? 2 : 1);
+    ch = ngroups >= 2 ? 2 : 1;
     if ((ngroups + ch - 1) / ch > 16) ch = (ngroups + 15) / 16;
     tw = (ngroups + ch - 1) / ch;
   }
@@ -498,12 +735,9 @@ int launch_prepare(const PrepareArgs &a0, cudaStream_t stream) {
   a.rows_per_block = rpb;
   const int threads = tw * 32 * rpb;
   const int64_t nblk = (a.rows + rpb - 1) / rpb;
-  const size_t smem = (tab ? kSiluEntries * 2 : 0) + sizeof(float) * 4 * (size_t)(tw * rpb);
-  if (nblk == 0) return 0;
-  bool ok = kind == KIND_PLAIN        ? launch_kind<KIND_PLAIN>(ch, a, threads, smem, nblk, stream)
-            : kind == KIND_SILU_TABLE ? launch_kind<KIND_SILU_TABLE>(ch, a, threads, smem, nblk, stream)
-                                      : launch_kind<KIND_GENERAL>(ch, a, threads, smem, nblk, stream);
-  if (!ok) return report_error(CLEFQ_ERR_SHAPE, "prepare: no kernel for this row width");
+  const size_t smem = sizeof(float) * 4 * (size_t)(tw * rpb);
+  if (!launch_kind<KIND_GENERAL>(ch, a, threads, smem, nblk, stream))
+    return report_error(CLEFQ_ERR_SHAPE, "prepare: no kernel for this row width");
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : report_error(CLEFQ_ERR_CUDA, cudaGetErrorString(e));
 }
