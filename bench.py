@@ -313,15 +313,24 @@ def run_clefq(args, world, rank, local):
     # ---- secondary workload: the C4 MoE layer (8192 tokens, 128 experts, top-8) --------
     moe = None
     if not args.skip_moe:
-        mg = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
-        mu = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
-        md = rand_weight_dev(clefq, MOE_E * MOE_H, MOE_I, gen)
         mx = torch.randn(MOE_T, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
         wr = torch.randn(MOE_E, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
         logits = mx @ wr.t()     # router linear (BF16, cuBLAS): outside the INT4 path
-        mws = torch.empty(clefq.lib().clefq_moe_workspace_size(MOE_T, MOE_H, MOE_I, MOE_E, MOE_K), dtype=torch.uint8,
-                          device="cuda")
-        mstep = lambda: clefq.omni_moe(mx, logits, mg, mu, md, workspace=mws)   # noqa: E731
+        if world > 1:
+            # expert parallel: this rank owns MOE_E / world experts and its own MOE_T tokens
+            from clefq.ep import ExpertShard, omni_moe_ep
+            per = MOE_E // world
+            shard = ExpertShard(rand_weight_dev(clefq, per * MOE_I, MOE_H, gen),
+                                rand_weight_dev(clefq, per * MOE_I, MOE_H, gen),
+                                rand_weight_dev(clefq, per * MOE_H, MOE_I, gen), rank * per, per, MOE_E, MOE_I)
+            mstep = lambda: omni_moe_ep(mx, logits, shard, MOE_K)   # noqa: E731
+        else:
+            mg = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
+            mu = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
+            md = rand_weight_dev(clefq, MOE_E * MOE_H, MOE_I, gen)
+            mws = torch.empty(clefq.lib().clefq_moe_workspace_size(MOE_T, MOE_H, MOE_I, MOE_E, MOE_K),
+                              dtype=torch.uint8, device="cuda")
+            mstep = lambda: clefq.omni_moe(mx, logits, mg, mu, md, workspace=mws)   # noqa: E731
         for _ in range(3):
             mstep()
         torch.cuda.synchronize()
@@ -329,8 +338,10 @@ def run_clefq(args, world, rank, local):
         mt = time_steps(mstep, max(5, min(args.steps, 30)), flush)
         mms = all_max(world, sum(mt) / len(mt))
         ops = 2.0 * MOE_T * MOE_K * (MOE_H * 2 * MOE_I + MOE_I * MOE_H)
-        moe = {"workload": "C4 Omni INT4 MoE layer: 8192 tokens, hidden 2048, 128 experts x (gate|up 2048->2x768, "
-                           "down 768->2048), top-8", "tokens_per_s": world * MOE_T / (mms / 1000), "ms_per_step": mms,
+        moe = {"workload": "C4 Omni INT4 MoE layer: 8192 tokens per GPU, hidden 2048, 128 experts x (gate|up "
+                           "2048->2x768, down 768->2048), top-8",
+               "parallelism": f"ep{world} (experts sharded, NCCL all-to-all dispatch/combine)" if world > 1
+               else "single GPU", "tokens_per_s": world * MOE_T / (mms / 1000), "ms_per_step": mms,
                "tops": ops / (mms / 1000) / 1e12, "frac_of_int8_peak": ops / (mms / 1000) / 1e12 / i8_peak}
 
     launches = 4 * args.steps

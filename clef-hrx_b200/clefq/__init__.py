@@ -48,6 +48,13 @@ _SYMBOLS = {
     "clefq_moe_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i", "i"]),
     "clefq_moe": (ctypes.c_int, ["p", "p", "p", "i", "l", "l", "l", "i", "i", "p", "p", "p", "p", "p", "p", "p", "p",
                                  "p", "l"]),
+    "clefq_moe_ep_record_bytes": (ctypes.c_int64, ["l"]),
+    "clefq_moe_ep_plan": (ctypes.c_int, ["p", "p", "l", "i", "i", "i", "p", "p"]),
+    "clefq_moe_ep_pack": (ctypes.c_int, ["p", "p", "l", "p", "l", "l", "p", "i", "p", "p"]),
+    "clefq_moe_ep_experts_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i"]),
+    "clefq_moe_ep_experts": (ctypes.c_int, ["p", "p", "l", "l", "l", "i", "i", "p", "p", "p", "p", "p", "p", "p", "p",
+                                            "l"]),
+    "clefq_moe_ep_combine": (ctypes.c_int, ["p", "p", "p", "p", "l", "i", "l", "p"]),
 }
 _CT = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64}
 

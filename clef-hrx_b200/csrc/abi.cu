@@ -22,6 +22,17 @@ int launch_gather_unpack_i4(const uint32_t *a, int64_t a_ld, const int *perm, in
                             uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms);
 int launch_combine(const uint16_t *values, const float *routes, const float *order, int64_t tokens, int topk,
                    int64_t width, uint16_t *out, cudaStream_t stream, int num_sms);
+int launch_ep_plan(const float *routes, int64_t tokens, int topk, int experts, int world, long long *counts,
+                   int *slots, cudaStream_t stream, int num_sms);
+int launch_ep_pack(const uint32_t *xq, int64_t words_ld, const float *scales, const float *routes, const int *slots,
+                   int64_t tokens, int topk, int code_words, int64_t rec_words, uint32_t *send, cudaStream_t stream,
+                   int num_sms);
+int launch_ep_unpack_meta(const uint32_t *recv, int64_t n, int code_words, int64_t rec_words, int expert_base,
+                          int local_experts, float *scales, float *routes, cudaStream_t stream, int num_sms);
+int launch_ep_weigh(const uint16_t *values, const float *routes, int64_t n, int64_t width, uint16_t *products,
+                    cudaStream_t stream, int num_sms);
+int launch_ep_combine(const uint16_t *products, const int *slots, const float *routes, int64_t tokens, int topk,
+                      int64_t width, uint16_t *out, cudaStream_t stream, int num_sms);
 
 // Status word set by bounded device-side waits (static: nothing is allocated for it).
 static __device__ int g_status_word;
@@ -455,6 +466,67 @@ int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t in
                   nullptr, nullptr, (int)(hidden / 128), hidden, inter, residual, hidden, CLEFQ_BF16, out, hidden);
 }
 
+// ---- grouped expert FFN shared by the fused MoE block and the expert-parallel path ----
+// xs: expert-sorted s8 operand rows (route order given by perm); a_scales: the token
+// scale of route r at a_scales[r / topk].  Writes values[route] = down(SwiGLU(gate|up)).
+static int run_expert_ffn(cudaStream_t s, const uint8_t *xs, int64_t nroutes, const float *a_scales, int topk,
+                          const int *tiles, const int *offsets, const int *perm, int experts, int tile_rows,
+                          int64_t hidden, int64_t inter, const void *gate_tiled, const float *gate_scales,
+                          const void *up_tiled, const float *up_scales, const void *down_tiled,
+                          const float *down_scales, uint16_t *gu, uint32_t *hq, uint8_t *h8, uint16_t *values) {
+  int *status = device_status_word();
+  if (!status) return cuda_err("status word");
+  GemmParams p{};
+  p.a_op = xs;
+  p.a_rows = nroutes;
+  p.a_ld = hidden;
+  p.a_scales = a_scales;
+  p.w[0] = static_cast<const uint32_t *>(gate_tiled);
+  p.w[1] = static_cast<const uint32_t *>(up_tiled);
+  p.w_scales[0] = gate_scales;
+  p.w_scales[1] = up_scales;
+  p.n_split = (int)(inter / 128);
+  p.n = (int)(2 * inter);
+  p.k = (int)hidden;
+  p.bits = 4;
+  p.out = gu;
+  p.ldo = 2 * inter;
+  p.grouped = 1;
+  p.tile_list = tiles;
+  p.expert_offsets = offsets;
+  p.perm = perm;
+  p.max_tiles = (int)((nroutes + tile_rows - 1) / tile_rows + experts);
+  p.experts = experts;
+  p.tile_rows = tile_rows;
+  p.topk = topk;
+  p.scale_mode = 1;  // activation scale of the token
+  p.scatter = 0;     // rows stay in expert-sorted order
+  p.err = status;
+  int rc = launch_gemm(p, s);
+  if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert gate/up launch") : set_err(rc, "expert gate/up shape");
+  // SwiGLU fused into the packing of the hidden rows (still expert-sorted).
+  rc = run_prepare(s, CLEFQ_PREP_SWIGLU, 4, gu, 2 * inter, gu + inter, 2 * inter, nroutes, inter, inter, hq, h8, inter,
+                   nullptr, 0);
+  if (rc) return rc;
+  p.a_op = h8;
+  p.a_ld = inter;
+  p.a_scales = reinterpret_cast<const float *>(hq + nroutes * (inter / 8));
+  p.w[0] = static_cast<const uint32_t *>(down_tiled);
+  p.w[1] = nullptr;
+  p.w_scales[0] = down_scales;
+  p.w_scales[1] = nullptr;
+  p.n_split = (int)(hidden / 128);
+  p.n = (int)hidden;
+  p.k = (int)inter;
+  p.out = values;
+  p.ldo = hidden;
+  p.scale_mode = 0;  // hidden rows were packed in sorted order
+  p.scatter = 1;     // values land at their route id
+  rc = launch_gemm(p, s);
+  if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert down launch") : set_err(rc, "expert down shape");
+  return 0;
+}
+
 // ---- fused Omni MoE block --------------------------------------------------------------
 struct MoeTables {
   float *routes, *order;
@@ -518,58 +590,123 @@ int clefq_moe(void *stream, const void *x, const void *logits, int logits_dtype,
   if (rc) return rc;
   rc = launch_gather(t.x8, hidden, t.perm, topk, nroutes, hidden, t.xs, hidden, s, sms);
   if (rc) return cuda_err("gather launch");
-  int *status = device_status_word();
-  if (!status) return cuda_err("status word");
-  GemmParams p{};
-  p.a_op = t.xs;
-  p.a_rows = nroutes;
-  p.a_ld = hidden;
-  p.a_scales = reinterpret_cast<const float *>(t.xq + tokens * (sh / 8));
-  p.w[0] = static_cast<const uint32_t *>(gate_tiled);
-  p.w[1] = static_cast<const uint32_t *>(up_tiled);
-  p.w_scales[0] = gate_scales;
-  p.w_scales[1] = up_scales;
-  p.n_split = (int)(inter / 128);
-  p.n = (int)(2 * inter);
-  p.k = (int)hidden;
-  p.bits = 4;
-  p.out = t.gu;
-  p.ldo = 2 * inter;
-  p.grouped = 1;
-  p.tile_list = t.tiles;
-  p.expert_offsets = t.offsets;
-  p.perm = t.perm;
-  p.max_tiles = (int)((nroutes + tile_rows - 1) / tile_rows + experts);
-  p.experts = experts;
-  p.tile_rows = tile_rows;
-  p.topk = topk;
-  p.scale_mode = 1;  // activation scale of the token
-  p.scatter = 0;     // rows stay in expert-sorted order
-  p.err = status;
-  rc = launch_gemm(p, s);
-  if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert gate/up launch") : set_err(rc, "expert gate/up shape");
-  // SwiGLU fused into the packing of the hidden rows (still expert-sorted).
-  rc = run_prepare(s, CLEFQ_PREP_SWIGLU, 4, t.gu, 2 * inter, t.gu + inter, 2 * inter, nroutes, inter, inter, t.hq, t.h8,
-                   inter, nullptr, 0);
+  rc = run_expert_ffn(s, t.xs, nroutes, reinterpret_cast<const float *>(t.xq + tokens * (sh / 8)), topk, t.tiles,
+                      t.offsets, t.perm, experts, tile_rows, hidden, inter, gate_tiled, gate_scales, up_tiled,
+                      up_scales, down_tiled, down_scales, t.gu, t.hq, t.h8, t.values);
   if (rc) return rc;
-  p.a_op = t.h8;
-  p.a_ld = inter;
-  p.a_scales = reinterpret_cast<const float *>(t.hq + nroutes * (inter / 8));
-  p.w[0] = static_cast<const uint32_t *>(down_tiled);
-  p.w[1] = nullptr;
-  p.w_scales[0] = down_scales;
-  p.w_scales[1] = nullptr;
-  p.n_split = (int)(hidden / 128);
-  p.n = (int)hidden;
-  p.k = (int)inter;
-  p.out = t.values;
-  p.ldo = hidden;
-  p.scale_mode = 0;  // hidden rows were packed in sorted order
-  p.scatter = 1;     // values land at their route id
-  rc = launch_gemm(p, s);
-  if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert down launch") : set_err(rc, "expert down shape");
   rc = launch_combine(t.values, routes, t.order, tokens, topk, hidden, static_cast<uint16_t *>(out), s, sms);
   return rc ? cuda_err("combine launch") : 0;
+}
+
+
+// ---- expert-parallel Omni MoE ----------------------------------------------------------
+// No reference counterpart (the reference runs the layer on one GPU); the pieces around
+// the two all-to-all exchanges a host makes.  Record of one dispatched route: the token's
+// hidden/8 code words, its f32 scale, the global expert id, the probability, padding to
+// 16 bytes.
+int64_t clefq_moe_ep_record_bytes(int64_t hidden) { return ((hidden / 8 + 3) * 4 + 15) / 16 * 16; }
+
+static int check_ep_shape(int64_t tokens, int64_t hidden, int experts, int topk, int world) {
+  if (tokens < 0 || tokens > 1048576 || hidden % 256 || hidden < 256 || hidden > 32768 ||
+      !(topk > 0 && topk <= experts && experts <= 128 && topk <= 32) || world < 1 || world > 64 || experts % world)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported expert-parallel MoE shape");
+  return 0;
+}
+
+int clefq_moe_ep_plan(void *stream, const float *routes, int64_t tokens, int topk, int experts, int world,
+                      int64_t *send_counts, int32_t *send_slots) {
+  int rc = check_ep_shape(tokens, 256, experts, topk, world);
+  if (rc) return rc;
+  if (tokens > 0 && (!routes || !send_slots)) return set_err(CLEFQ_ERR_SHAPE, "null routes or slots");
+  if (!send_counts) return set_err(CLEFQ_ERR_SHAPE, "null send counts");
+  rc = launch_ep_plan(routes, tokens, topk, experts, world, reinterpret_cast<long long *>(send_counts), send_slots,
+                      static_cast<cudaStream_t>(stream), device_sms());
+  return rc ? cuda_err("expert-parallel plan launch") : 0;
+}
+
+int clefq_moe_ep_pack(void *stream, const void *a_codes, int64_t a_ld_words, const float *a_scales, int64_t tokens,
+                      int64_t hidden, const float *routes, int topk, const int32_t *send_slots, void *send_records) {
+  int rc = check_ep_shape(tokens, hidden, topk, topk, 1);
+  if (rc) return rc;
+  if (a_ld_words < hidden / 8 || (a_ld_words & 3) || !al16(a_codes) || !al16(send_records))
+    return set_err(CLEFQ_ERR_ALIGN, "codes and records must be 16-byte aligned rows");
+  rc = launch_ep_pack(static_cast<const uint32_t *>(a_codes), a_ld_words, a_scales, routes, send_slots, tokens, topk,
+                      (int)(hidden / 8), clefq_moe_ep_record_bytes(hidden) / 4, static_cast<uint32_t *>(send_records),
+                      static_cast<cudaStream_t>(stream), device_sms());
+  return rc ? cuda_err("expert-parallel pack launch") : 0;
+}
+
+struct EpTables {
+  float *routes, *scales;
+  int *counts, *offsets, *tiles, *perm;
+  uint8_t *xs, *h8;
+  uint16_t *gu, *values;
+  uint32_t *hq;
+};
+static Arena ep_tables(Arena a, int64_t n, int64_t hidden, int64_t inter, int local_experts, EpTables &t) {
+  const int64_t rows = n > 0 ? n : 1;
+  t.routes = a.take<float>(2 * rows);
+  t.scales = a.take<float>(rows);
+  t.counts = a.take<int>(local_experts);
+  t.offsets = a.take<int>(local_experts + 1);
+  t.tiles = a.take<int>(1 + 2 * ((rows + 127) / 128 + local_experts));
+  t.perm = a.take<int>(rows);
+  t.xs = a.take<uint8_t>(rows * hidden);
+  t.gu = a.take<uint16_t>(rows * 2 * inter);
+  t.hq = a.take<uint32_t>(rows * (inter / 8 + 1));
+  t.h8 = a.take<uint8_t>(rows * inter);
+  t.values = a.take<uint16_t>(rows * hidden);
+  return a;
+}
+
+int64_t clefq_moe_ep_experts_workspace_size(int64_t records, int64_t hidden, int64_t inter, int local_experts) {
+  EpTables t;
+  Arena a{nullptr, INT64_MAX};
+  a = ep_tables(a, records, hidden, inter, local_experts, t);
+  return aligned_total(a);
+}
+
+int clefq_moe_ep_experts(void *stream, const void *records, int64_t n, int64_t hidden, int64_t inter, int expert_base,
+                         int local_experts, const void *gate_tiled, const float *gate_scales, const void *up_tiled,
+                         const float *up_scales, const void *down_tiled, const float *down_scales, void *products,
+                         void *workspace, int64_t workspace_bytes) {
+  if (n < 0 || n > 32 * 1048576 || hidden % 256 || inter % 256 || hidden < 256 || inter < 256 || hidden > 32768 ||
+      inter > 32768 || local_experts < 1 || local_experts > 128 || expert_base < 0)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported expert-parallel expert shape");
+  if (n == 0) return 0;
+  if (!al16(records) || !al16(products)) return set_err(CLEFQ_ERR_ALIGN, "records and products must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  EpTables t;
+  Arena a = ep_tables(Arena{static_cast<uint8_t *>(workspace), workspace_bytes}, n, hidden, inter, local_experts, t);
+  if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "expert-parallel workspace too small");
+  const int sms = device_sms();
+  const int tile_rows = gemm_tile_rows((int)(2 * inter), (int)(inter / 128));
+  if (gemm_tile_rows((int)hidden, (int)(hidden / 128)) != tile_rows)
+    return set_err(CLEFQ_ERR_SHAPE, "hidden and intermediate must both be multiples of 256, or neither");
+  const int code_words = (int)(hidden / 8);
+  const int64_t rec_words = clefq_moe_ep_record_bytes(hidden) / 4;
+  const uint32_t *recv = static_cast<const uint32_t *>(records);
+  int rc = launch_ep_unpack_meta(recv, n, code_words, rec_words, expert_base, local_experts, t.scales, t.routes, s, sms);
+  if (!rc)
+    rc = launch_group(t.routes, n, 1, local_experts, tile_rows, t.counts, t.offsets, t.tiles, t.perm, nullptr, nullptr,
+                      nullptr, s, sms);
+  if (!rc) rc = launch_gather_unpack_i4(recv, rec_words, t.perm, 1, n, (int)hidden, t.xs, hidden, s, sms);
+  if (rc) return cuda_err("expert-parallel grouping launch");
+  rc = run_expert_ffn(s, t.xs, n, t.scales, 1, t.tiles, t.offsets, t.perm, local_experts, tile_rows, hidden, inter,
+                      gate_tiled, gate_scales, up_tiled, up_scales, down_tiled, down_scales, t.gu, t.hq, t.h8, t.values);
+  if (rc) return rc;
+  rc = launch_ep_weigh(t.values, t.routes, n, hidden, static_cast<uint16_t *>(products), s, sms);
+  return rc ? cuda_err("expert-parallel weigh launch") : 0;
+}
+
+int clefq_moe_ep_combine(void *stream, const void *products, const int32_t *send_slots, const float *routes,
+                         int64_t tokens, int topk, int64_t hidden, void *out) {
+  int rc = check_ep_shape(tokens, hidden, topk, topk, 1);
+  if (rc) return rc;
+  if (!al16(products) || !al16(out)) return set_err(CLEFQ_ERR_ALIGN, "products and output must be 16-byte aligned");
+  rc = launch_ep_combine(static_cast<const uint16_t *>(products), send_slots, routes, tokens, topk, hidden,
+                         static_cast<uint16_t *>(out), static_cast<cudaStream_t>(stream), device_sms());
+  return rc ? cuda_err("expert-parallel combine launch") : 0;
 }
 
 }  // extern "C"

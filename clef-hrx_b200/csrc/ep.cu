@@ -1,0 +1,222 @@
+// clefq: expert-parallel Omni MoE helpers (routes sharded over GPUs by expert id).
+//
+// The reference runs the MoE layer on one GPU (src/omni.rs:761-857); these kernels split
+// it across ranks so that every rank keeps the experts [rank * E/G, (rank + 1) * E/G):
+//
+//   home rank:   route -> quantise each token once -> plan (one record per route, grouped
+//                by destination rank, in route order) -> pack records
+//   all-to-all:  records (int4 codes of the token, its f32 scale, expert id, probability)
+//   remote rank: grouped expert GEMMs on the received records -> bf16(value * probability)
+//   all-to-all:  per-route products back, in the order they were sent
+//   home rank:   the reference's ascending-expert BF16 chain over the returned products
+//
+// Every step that rounds is the single-GPU step on the same operands (rows are quantised
+// and multiplied independently; the chain runs on the home rank in the same order), so
+// the result is bit-identical to one GPU.
+#include "cq_common.cuh"
+#include "clefq_internal.h"
+
+namespace cq {
+
+// Routes per destination rank (expert / experts_per_rank).
+__global__ void ep_count_kernel(const float *__restrict__ routes, int64_t tokens, int topk, int per_rank, int world,
+                                long long *__restrict__ counts) {
+  const int64_t total = tokens * topk;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / topk;
+    const int r = (int)(i % topk);
+    const int e = (int)routes[t * 2 * topk + r];
+    const int d = e / per_rank;
+    if (e >= 0 && d < world) atomicAdd(reinterpret_cast<unsigned long long *>(&counts[d]), 1ull);
+  }
+}
+
+// One CTA (256 threads) per destination: the send slot of each of its routes, stable in
+// route order (token-major, then rank k), after all routes of lower destinations.
+__global__ void __launch_bounds__(256) ep_slot_kernel(const float *__restrict__ routes, int64_t tokens, int topk,
+                                                      int per_rank, const long long *__restrict__ counts,
+                                                      int *__restrict__ slots) {
+  __shared__ int warp_tot[8];
+  const int d = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long base = 0;
+  for (int q = 0; q < d; ++q) base += counts[q];
+  const int64_t total = tokens * topk;
+  long long count0 = 0;
+  for (int64_t i0 = 0; i0 < total; i0 += 256) {
+    const int64_t i = i0 + threadIdx.x;
+    bool match = false;
+    if (i < total) {
+      const int e = (int)routes[(i / topk) * 2 * topk + (i % topk)];
+      match = e >= 0 && e / per_rank == d;
+    }
+    const unsigned ballot = __ballot_sync(0xffffffffu, match);
+    const int in_warp = __popc(ballot & ((1u << lane) - 1u));
+    if (lane == 0) warp_tot[warp] = __popc(ballot);
+    __syncthreads();
+    int before = 0, tot = 0;
+    for (int w = 0; w < 8; ++w) {
+      const int n = warp_tot[w];
+      if (w < warp) before += n;
+      tot += n;
+    }
+    if (match) slots[i] = (int)(base + count0 + before + in_warp);
+    count0 += tot;
+    __syncthreads();
+  }
+}
+
+int launch_ep_plan(const float *routes, int64_t tokens, int topk, int experts, int world, long long *counts,
+                   int *slots, cudaStream_t stream, int num_sms) {
+  if (world < 1 || world > 64 || experts % world) return CLEFQ_ERR_SHAPE;
+  const int per_rank = experts / world;
+  cudaMemsetAsync(counts, 0, sizeof(long long) * world, stream);
+  const int64_t total = tokens * topk;
+  if (total > 0) {
+    int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 8;
+    ep_count_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(routes, tokens, topk, per_rank, world,
+                                                                                 counts);
+    ep_slot_kernel<<<world, 256, 0, stream>>>(routes, tokens, topk, per_rank, counts, slots);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+}
+
+// One warp per route: the token's packed code row (hidden/8 words), then scale, expert id
+// and probability, at record slots[route] of the send buffer.
+__global__ void ep_pack_kernel(const uint32_t *__restrict__ xq, int64_t words_ld, const float *__restrict__ scales,
+                               const float *__restrict__ routes, const int *__restrict__ slots, int64_t tokens,
+                               int topk, int code_words, int64_t rec_words, uint32_t *__restrict__ send) {
+  const int lane = threadIdx.x & 31;
+  const int64_t total = tokens * topk;
+  const int64_t wstride = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t i = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += wstride) {
+    const int64_t t = i / topk;
+    const int r = (int)(i % topk);
+    uint32_t *rec = send + (int64_t)slots[i] * rec_words;
+    const uint32_t *src = xq + t * words_ld;
+    for (int w = lane * 4; w < code_words; w += 128)
+      *reinterpret_cast<uint4 *>(rec + w) = *reinterpret_cast<const uint4 *>(src + w);
+    if (lane == 0) {
+      rec[code_words] = __float_as_uint(scales[t]);
+      rec[code_words + 1] = (uint32_t)(int)routes[t * 2 * topk + r];
+      rec[code_words + 2] = __float_as_uint(routes[t * 2 * topk + topk + r]);
+      rec[code_words + 3] = 0u;
+    }
+  }
+}
+
+int launch_ep_pack(const uint32_t *xq, int64_t words_ld, const float *scales, const float *routes, const int *slots,
+                   int64_t tokens, int topk, int code_words, int64_t rec_words, uint32_t *send, cudaStream_t stream,
+                   int num_sms) {
+  const int64_t total = tokens * topk;
+  if (total == 0) return 0;
+  int64_t blocks = (total + 7) / 8, cap = (int64_t)num_sms * 16;
+  ep_pack_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(xq, words_ld, scales, routes, slots,
+                                                                              tokens, topk, code_words, rec_words, send);
+  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+}
+
+// Received records -> contiguous activation scales and one-route-per-record routes
+// (local expert id, probability) in the [rows][2] layout the grouping kernels read.
+// Records whose expert is not local get id -1 and are left out of every group.
+__global__ void ep_unpack_meta_kernel(const uint32_t *__restrict__ recv, int64_t n, int code_words, int64_t rec_words,
+                                      int expert_base, int local_experts, float *__restrict__ scales,
+                                      float *__restrict__ routes) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t *rec = recv + i * rec_words;
+    const int e = (int)rec[code_words + 1] - expert_base;
+    scales[i] = __uint_as_float(rec[code_words]);
+    routes[2 * i] = (float)(e >= 0 && e < local_experts ? e : -1);
+    routes[2 * i + 1] = __uint_as_float(rec[code_words + 2]);
+  }
+}
+
+int launch_ep_unpack_meta(const uint32_t *recv, int64_t n, int code_words, int64_t rec_words, int expert_base,
+                          int local_experts, float *scales, float *routes, cudaStream_t stream, int num_sms) {
+  if (n == 0) return 0;
+  int64_t blocks = (n + 255) / 256, cap = (int64_t)num_sms * 8;
+  ep_unpack_meta_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(
+      recv, n, code_words, rec_words, expert_base, local_experts, scales, routes);
+  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+}
+
+// products[i] = bf16(bf16(values[i]) * probability of record i): the per-route term of the
+// reference's combine (src/omni.rs:512-557), eight columns per thread.
+__global__ void ep_weigh_kernel(const uint16_t *__restrict__ values, const float *__restrict__ routes, int64_t n,
+                                int64_t width, uint16_t *__restrict__ products) {
+  const int64_t per_row = width / 8;
+  const int64_t total = n * per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / per_row;
+    const int64_t c = (i % per_row) * 8;
+    const float p = routes[2 * row + 1];
+    const uint4 raw = *reinterpret_cast<const uint4 *>(values + row * width + c);
+    const uint16_t *h = reinterpret_cast<const uint16_t *>(&raw);
+    uint4 o;
+    uint16_t *oh = reinterpret_cast<uint16_t *>(&o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) oh[q] = f32_to_bf16(__fmul_rn(bf16_to_f32(h[q]), p));
+    *reinterpret_cast<uint4 *>(products + row * width + c) = o;
+  }
+}
+
+int launch_ep_weigh(const uint16_t *values, const float *routes, int64_t n, int64_t width, uint16_t *products,
+                    cudaStream_t stream, int num_sms) {
+  const int64_t total = n * (width / 8);
+  if (total == 0) return 0;
+  int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
+  ep_weigh_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(values, routes, n, width, products);
+  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+}
+
+// Home rank: out[t] = the ascending-expert chain s = bf16(s + product) over the token's
+// routes, each product found at its send slot (the products come back in send order).
+__global__ void ep_combine_kernel(const uint16_t *__restrict__ products, const int *__restrict__ slots,
+                                  const float *__restrict__ routes, int64_t tokens, int topk, int64_t width,
+                                  uint16_t *__restrict__ out) {
+  const int64_t per_tok = width / 8;
+  const int64_t total = tokens * per_tok;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / per_tok;
+    const int64_t c = (i % per_tok) * 8;
+    const float *rt = routes + t * 2 * topk;
+    float s[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s[q] = 0.0f;
+    float prev = -1.0f;
+    for (int j = 0; j < topk; ++j) {
+      // next larger expert id (the reference's combine order; ids are distinct)
+      float best = 1000000.0f;
+      int r = 0;
+      for (int q = 0; q < topk; ++q) {
+        const float e = rt[q];
+        if (e > prev && e < best) {
+          best = e;
+          r = q;
+        }
+      }
+      prev = best;
+      const uint4 raw = *reinterpret_cast<const uint4 *>(products + (int64_t)slots[t * topk + r] * width + c);
+      const uint16_t *h = reinterpret_cast<const uint16_t *>(&raw);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) s[q] = bf16r(__fadd_rn(s[q], bf16_to_f32(h[q])));
+    }
+    uint4 o;
+    uint16_t *oh = reinterpret_cast<uint16_t *>(&o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) oh[q] = f32_to_bf16(s[q]);
+    *reinterpret_cast<uint4 *>(out + t * width + c) = o;
+  }
+}
+
+int launch_ep_combine(const uint16_t *products, const int *slots, const float *routes, int64_t tokens, int topk,
+                      int64_t width, uint16_t *out, cudaStream_t stream, int num_sms) {
+  const int64_t total = tokens * (width / 8);
+  if (total == 0) return 0;
+  int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
+  ep_combine_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(products, slots, routes, tokens, topk,
+                                                                                 width, out);
+  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+}
+
+}  // namespace cq

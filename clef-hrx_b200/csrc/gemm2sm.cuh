@@ -7,8 +7,9 @@
 //   * each CTA TMA-loads its own 96 token rows (the B operand is split along N between the
 //     pair's shared memory); the loads use the .cta_group::2 form so that both halves count
 //     on the leader's barrier -- plain loads, no multicast,
-//   * the leader issues tcgen05.mma.cta_group::2 (M=256, N=192, K=32) and multicasts each
-//     completion (tcgen05.commit) to both CTAs,
+//   * the leader issues tcgen05.mma.cta_group::2 (M=256, N=192, K=32) and multicasts one
+//     completion (tcgen05.commit) per K stage to both CTAs: it frees the stage's token slot
+//     and tells the converters that the TMEM weight stage of two K stages back is free,
 //   * both CTAs drain their 128-row slice of the accumulator; accumulators are double
 //     buffered (2 x 192 TMEM columns) so a tile's epilogue overlaps the next mainloop.
 // Per SM this moves 40 KB of operands per 768 MMA cycles (~53 B/clk), under the ~67 B/clk
@@ -35,18 +36,24 @@ constexpr int TMA_W = 4, MMA_W = 5;
 constexpr uint32_t IDESC2 = idesc_i8(256, BN2);
 constexpr int STAGING2 = BN2 * 128 * 2;        // 48 KiB BF16 [token][column]
 
+// Separate rings for the two operands.  Token slots are held until the MMAs that read
+// them complete, so their ring must cover the TMA latency (~3k cycles under load) plus a
+// stage: 5 slots.  Weight slots are copied into registers by the converters as soon as
+// they land (before waiting for a free TMEM stage), so 3 slots keep them ahead.
 template <int BITS>
 struct Cfg2 {
-  static constexpr int NS = BITS == 4 ? 4 : 3;
+  static constexpr int NT = BITS == 4 ? 5 : 4;            // token stages (24 KiB each)
+  static constexpr int NW = BITS == 4 ? 3 : 2;            // weight stages
   static constexpr int W_BYTES = 128 * KS2 * BITS / 8;
-  static constexpr int STAGE = TOK_B + W_BYTES;
-  static constexpr int SMEM = NS * STAGE + STAGING2 + 1024 + 1024;
+  static constexpr int W_OFF = NT * TOK_B;                // weight ring after the token ring
+  static constexpr int RING = NT * TOK_B + NW * W_BYTES;
+  static constexpr int SMEM = RING + STAGING2 + 1024 + 1024;
 };
 
-template <int NS>
+template <int NT, int NW>
 struct Smem2 {
-  uint64_t tok_full[NS], tok_empty[NS], wsm_full[NS], wsm_empty[NS];
-  uint64_t wtm_full[NSW], wtm_empty[NSW], acc_full[2], acc_empty[2];
+  uint64_t tok_full[NT], tok_empty[NT], wsm_full[NW], wsm_empty[NW];
+  uint64_t wtm_full[NSW], acc_full[2], acc_empty[2];
   uint32_t sink[4 + EPI_WARPS];  // targets of the follower's asynchronous 4-byte signals
   uint32_t tmem_base;
   int err;
@@ -77,12 +84,12 @@ __global__ void __launch_bounds__(THREADS2, 1)
     gemm_i8_2sm_kernel(const __grid_constant__ CUtensorMap tok_map, const __grid_constant__ CUtensorMap w_map0,
                        const __grid_constant__ CUtensorMap w_map1, GemmParams p) {
   using C = Cfg2<BITS>;
-  constexpr int NS = C::NS;
+  constexpr int NT = C::NT, NW = C::NW;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t *ring = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  uint16_t *staging = reinterpret_cast<uint16_t *>(ring + NS * C::STAGE);
-  Smem2<NS> &s = *reinterpret_cast<Smem2<NS> *>(ring + NS * C::STAGE + STAGING2);
+  uint16_t *staging = reinterpret_cast<uint16_t *>(ring + C::RING);
+  Smem2<NT, NW> &s = *reinterpret_cast<Smem2<NT, NW> *>(ring + C::RING + STAGING2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
@@ -95,18 +102,17 @@ __global__ void __launch_bounds__(THREADS2, 1)
   const int blocks_k = p.k / (32 * (32 / BITS));
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NS; ++i) {
+    for (int i = 0; i < NT; ++i) {
       mbar_init(&s.tok_full[i], 1);
       mbar_init(&s.tok_empty[i], 1);
+    }
+    for (int i = 0; i < NW; ++i) {
       mbar_init(&s.wsm_full[i], 1);
       mbar_init(&s.wsm_empty[i], 128);
     }
     // wtm_full / acc_empty (used on the leader): 4 local warp arrivals, one of which
     // also expects the follower's 4 x 4 signal bytes (st.async complete_tx).
-    for (int i = 0; i < NSW; ++i) {
-      mbar_init(&s.wtm_full[i], 4);
-      mbar_init(&s.wtm_empty[i], 1);
-    }
+    for (int i = 0; i < NSW; ++i) mbar_init(&s.wtm_full[i], 4);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
       mbar_init(&s.acc_empty[i], EPI_WARPS);
@@ -150,19 +156,18 @@ __global__ void __launch_bounds__(THREADS2, 1)
         const int k_off = (int)((7u * (uint32_t)t) % (uint32_t)k_stages);
         for (int kk = 0; kk < k_stages; ++kk, ++g) {
           const int kb = kk + k_off < k_stages ? kk + k_off : kk + k_off - k_stages;
-          const int st = g % NS;
-          const uint32_t ph = ((g / NS) & 1) ^ 1;
-          if (!(ok = mbar_wait_bounded(&s.tok_empty[st], ph, &s.err, 1) &&
-                     mbar_wait_bounded(&s.wsm_empty[st], ph, &s.err, 1)))
-            break;
-          uint8_t *stage = ring + st * C::STAGE;
-          if (rank == 0) mbar_arrive_expect_tx(&s.tok_full[st], 2 * TOK_B);
+          const int sw = g % NW, st = g % NT;
+          // weight box first (its slot frees as soon as the converters have read it):
+          // whole 128-row x 32-word tiled block(s) of this K=256 slice
+          if (!(ok = mbar_wait_bounded(&s.wsm_empty[sw], ((g / NW) & 1) ^ 1, &s.err, 1))) break;
+          mbar_arrive_expect_tx(&s.wsm_full[sw], C::W_BYTES);
+          tma_load_3d(ring + C::W_OFF + sw * C::W_BYTES, w_map, &s.wsm_full[sw], 0, 0,
+                      w_row_tile * blocks_k + kb * (BITS == 4 ? 1 : 2));
           // token box: x = 128 bytes of a K slice, y = 96 rows, z = the stage's two K slices
-          tma_load_3d_cg2(stage, &tok_map, mapa_shared(smem_u32(&s.tok_full[st]), 0), 0, (int)(row0 + HALF * rank),
-                          2 * kb);
-          mbar_arrive_expect_tx(&s.wsm_full[st], C::W_BYTES);
-          // weight box: whole 128-row x 32-word tiled block(s) of this K=256 slice
-          tma_load_3d(stage + TOK_B, w_map, &s.wsm_full[st], 0, 0, w_row_tile * blocks_k + kb * (BITS == 4 ? 1 : 2));
+          if (!(ok = mbar_wait_bounded(&s.tok_empty[st], ((g / NT) & 1) ^ 1, &s.err, 1))) break;
+          if (rank == 0) mbar_arrive_expect_tx(&s.tok_full[st], 2 * TOK_B);
+          tma_load_3d_cg2(ring + st * TOK_B, &tok_map, mapa_shared(smem_u32(&s.tok_full[st]), 0), 0,
+                          (int)(row0 + HALF * rank), 2 * kb);
         }
       }
     }
@@ -180,19 +185,18 @@ __global__ void __launch_bounds__(THREADS2, 1)
         tc_fence_after();
         const uint32_t acc = tmem + ACC_COLS * buf;
         for (int kb = 0; kb < k_stages; ++kb, ++g) {
-          const int st = g % NS;
+          const int st = g % NT;
           const int sw = g % NSW;
-          if (!(ok = mbar_wait_bounded(&s.tok_full[st], (g / NS) & 1, &s.err, 2) &&
+          if (!(ok = mbar_wait_bounded(&s.tok_full[st], (g / NT) & 1, &s.err, 2) &&
                      mbar_wait_bounded(&s.wtm_full[sw], (g / NSW) & 1, &s.err, 3)))
             break;
           tc_fence_after();
-          const uint32_t b_base = smem_u32(ring + st * C::STAGE);
+          const uint32_t b_base = smem_u32(ring + st * TOK_B);
 #pragma unroll
           for (int j = 0; j < KS2 / 32; ++j)
             mma_i8_ts2(acc, tmem + WCOL + 64 * sw + 8 * j, smem_desc_sw128(b_base + (j >> 2) * (TOK_B / 2) + 32 * (j & 3)),
                        IDESC2, (kb | j) != 0);
           mma_commit2_mc(&s.tok_empty[st], 3);
-          mma_commit2_mc(&s.wtm_empty[sw], 3);
         }
         mma_commit2_mc(&s.acc_full[buf], 3);
       }
@@ -210,16 +214,13 @@ __global__ void __launch_bounds__(THREADS2, 1)
     int rows_valid, np, expert;
     for (int t = cluster; ok && tm.get(p, t, row0, rows_valid, np, expert); t += nclusters) {
       for (int kb = 0; kb < k_stages; ++kb, ++g) {
-        const int st = g % NS;
+        const int st = g % NW;
         const int sw = g % NSW;
         bool waited = true;
-        if (lane == 0)
-          waited = mbar_wait_bounded(&s.wsm_full[st], (g / NS) & 1, &s.err, 4) &&
-                   mbar_wait_bounded(&s.wtm_empty[sw], ((g / NSW) & 1) ^ 1, &s.err, 4);
+        if (lane == 0) waited = mbar_wait_bounded(&s.wsm_full[st], (g / NW) & 1, &s.err, 4);
         waited = __shfl_sync(0xffffffffu, waited, 0) != 0;
         if (!(ok = waited)) break;
-        tc_fence_after();
-        const uint32_t wbase = smem_u32(ring + st * C::STAGE + TOK_B);
+        const uint32_t wbase = smem_u32(ring + C::W_OFF + st * C::W_BYTES);
         // 128-byte rows, 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
         uint32_t w[32];
 #pragma unroll
@@ -236,6 +237,15 @@ __global__ void __launch_bounds__(THREADS2, 1)
           }
         }
         mbar_arrive(&s.wsm_empty[st]);
+        // the weights are in registers: now wait for the TMEM stage the MMA last read, i.e.
+        // for the MMAs of stage g - NSW, whose completion the token ring's commit reports
+        if (lane == 0 && g >= NSW) {
+          const uint32_t gp = g - NSW;
+          waited = mbar_wait_bounded(&s.tok_empty[gp % NT], (gp / NT) & 1, &s.err, 4);
+        }
+        waited = __shfl_sync(0xffffffffu, waited, 0) != 0;
+        if (!(ok = waited)) break;
+        tc_fence_after();
         if (BITS == 4) {
           // 8 words per 32-code group -> low nibbles then high nibbles (x16)
 #pragma unroll

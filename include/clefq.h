@@ -217,6 +217,41 @@ CLEFQ_API int clefq_moe(void *stream, const void *x, const void *logits, int log
                         const void *down_tiled, const float *down_scales, void *out, float *routes_out,
                         void *workspace, int64_t workspace_bytes);
 
+/*
+ * Expert-parallel Omni MoE.  No counterpart in the reference, which runs the MoE block on
+ * one GPU (src/omni.rs:761-857); these are the pieces around the two all-to-all exchanges
+ * of a host that shards the experts over `world` ranks (rank r owns experts
+ * [r*experts/world, (r+1)*experts/world)).  Per layer, on every rank:
+ *   1. clefq_route + clefq_prepare(x, int4, no operand)              (home tokens)
+ *   2. clefq_moe_ep_plan  -> send_counts[world] (int64, device) and send_slots[tokens*topk]
+ *   3. exchange counts; clefq_moe_ep_pack -> one record per route, grouped by destination
+ *   4. all-to-all of the records (clefq_moe_ep_record_bytes(hidden) bytes each)
+ *   5. clefq_moe_ep_experts on the received records -> BF16 products bf16(value * prob)
+ *   6. all-to-all of the products back (hidden BF16 each, same order as sent)
+ *   7. clefq_moe_ep_combine -> the reference's ascending-expert BF16 chain per token.
+ * The result is bit-identical to clefq_moe on one GPU.
+ */
+CLEFQ_API int64_t clefq_moe_ep_record_bytes(int64_t hidden);
+/* routes f32 [tokens][2*topk] from clefq_route; send_counts int64 [world]; send_slots int32 [tokens*topk] */
+CLEFQ_API int clefq_moe_ep_plan(void *stream, const float *routes, int64_t tokens, int topk, int experts, int world,
+                                int64_t *send_counts, int32_t *send_slots);
+/* a_codes/a_ld_words/a_scales: packed int4 rows of the tokens (clefq_prepare storage) */
+CLEFQ_API int clefq_moe_ep_pack(void *stream, const void *a_codes, int64_t a_ld_words, const float *a_scales,
+                                int64_t tokens, int64_t hidden, const float *routes, int topk,
+                                const int32_t *send_slots, void *send_records);
+/* records [n][record_bytes] received from all ranks; local expert weights as in clefq_moe with
+ * experts = local_experts; products BF16 [n][hidden] in record order. */
+CLEFQ_API int64_t clefq_moe_ep_experts_workspace_size(int64_t records, int64_t hidden, int64_t inter,
+                                                      int local_experts);
+CLEFQ_API int clefq_moe_ep_experts(void *stream, const void *records, int64_t n, int64_t hidden, int64_t inter,
+                                   int expert_base, int local_experts, const void *gate_tiled, const float *gate_scales,
+                                   const void *up_tiled, const float *up_scales, const void *down_tiled,
+                                   const float *down_scales, void *products, void *workspace,
+                                   int64_t workspace_bytes);
+/* products BF16 [sum(send_counts)][hidden] in send order; out BF16 [tokens][hidden] */
+CLEFQ_API int clefq_moe_ep_combine(void *stream, const void *products, const int32_t *send_slots, const float *routes,
+                                   int64_t tokens, int topk, int64_t hidden, void *out);
+
 #ifdef __cplusplus
 }
 #endif

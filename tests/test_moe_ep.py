@@ -1,0 +1,190 @@
+"""Expert-parallel Omni MoE: every rank's output equals the single-GPU layer bit for bit.
+
+- CPU, 2 gloo ranks: the real host orchestration (clefq.ep.omni_moe_ep) with the device
+  steps replaced by oracle stand-ins, against the oracle's single-process moe_layer
+  (src/omni.rs:761-857 semantics).
+- GPU, one process: G = 2 and 4 ranks simulated by splicing send/receive buffers exactly as
+  the two all-to-all exchanges do, through every libclefq expert-parallel entry point,
+  against clefq.omni_moe on the same tokens.
+- GPU, 2 processes over NCCL (needs two GPUs).
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+# ---------------------------------------------------------------------------------------
+# CPU: 2 gloo ranks, oracle stand-ins
+# ---------------------------------------------------------------------------------------
+CPU_T, CPU_H, CPU_I, CPU_E, CPU_K = 24, 256, 256, 8, 2
+
+
+def _cpu_problem():
+    from oracle import oracle as o
+    rng = np.random.default_rng(7)
+    world = 2
+    x = o.f32_to_bf16(rng.standard_normal((world * CPU_T, CPU_H)).astype(np.float32))
+    logits = o.f32_to_bf16(rng.standard_normal((world * CPU_T, CPU_E)).astype(np.float32))
+    gate = o.pack_weight(o.f32_to_bf16(rng.standard_normal((CPU_E * CPU_I, CPU_H)).astype(np.float32) * 0.05))
+    up = o.pack_weight(o.f32_to_bf16(rng.standard_normal((CPU_E * CPU_I, CPU_H)).astype(np.float32) * 0.05))
+    down = o.pack_weight(o.f32_to_bf16(rng.standard_normal((CPU_E * CPU_H, CPU_I)).astype(np.float32) * 0.05))
+    return x, logits, gate, up, down
+
+
+def _cpu_worker(rank, world, port):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
+    from oracle import oracle as o
+    from clefq.ep import ExpertShard, omni_moe_ep
+    from tests.ep_oracle_ops import OracleEpOps
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        x, logits, gate, up, down = _cpu_problem()
+        per = CPU_E // world
+        base = rank * per
+
+        def cut(w, rows_per_expert, cols):
+            words = cols // 8
+            lo, hi = base * rows_per_expert, (base + per) * rows_per_expert
+            return (w[0][lo * words:hi * words], w[1][lo:hi])
+        shard = ExpertShard(cut(gate, CPU_I, CPU_H), cut(up, CPU_I, CPU_H), cut(down, CPU_H, CPU_I), base, per, CPU_E,
+                            CPU_I)
+        mine = slice(rank * CPU_T, (rank + 1) * CPU_T)
+        xt = torch.from_numpy(x[mine].view(np.int16).copy()).view(torch.bfloat16)
+        lt = torch.from_numpy(logits[mine].view(np.int16).copy()).view(torch.bfloat16)
+        out, routes = omni_moe_ep(xt, lt, shard, CPU_K, ops=OracleEpOps())
+        # weight tuples: (tiled codes, scales, rows per expert)
+        ref, ref_routes, _, _ = o.moe_layer(x, logits, (gate[0], gate[1], CPU_I), (up[0], up[1], CPU_I),
+                                            (down[0], down[1], CPU_H), CPU_K, CPU_E)
+        got = out.view(torch.int16).numpy().view(np.uint16)
+        assert np.array_equal(routes.numpy(), ref_routes[mine])
+        assert np.array_equal(got, ref[mine]), f"rank {rank}: {np.count_nonzero(got != ref[mine])} mismatches"
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_host_logic_two_gloo_ranks():
+    mp.start_processes(_cpu_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
+
+
+def test_ep_record_bytes_matches_library_formula():
+    from tests.ep_oracle_ops import record_bytes
+    import clefq
+    for h in (256, 2048, 4096, 7168):
+        assert clefq.lib().clefq_moe_ep_record_bytes(h) == record_bytes(h)
+
+
+# ---------------------------------------------------------------------------------------
+# GPU, one process: simulated ranks
+# ---------------------------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def cq():
+    import clefq
+    clefq.lib()
+    return clefq
+
+
+def _weights(cq, experts, inter, hidden, seed):
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+
+    def w(rows, cols):
+        return cq.load_quantized_weight((torch.randn(rows, cols, device="cuda", generator=gen) * 0.05)
+                                        .to(torch.bfloat16))
+    return w(experts * inter, hidden), w(experts * inter, hidden), w(experts * hidden, inter)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,experts,topk,tokens", [(2, 16, 4, 100), (4, 16, 4, 37), (4, 128, 8, 300)])
+def test_ep_simulated_ranks_match_single_gpu(cq, world, experts, topk, tokens):
+    from clefq.ep import CudaEpOps, shard_experts
+    hidden, inter = 512, 256
+    gate, up, down = _weights(cq, experts, inter, hidden, 11)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(world * 100 + tokens)
+    xs = [torch.randn(tokens + 3 * h, hidden, device="cuda", generator=gen).to(torch.bfloat16) for h in range(world)]
+    ls = [torch.randn(tokens + 3 * h, experts, device="cuda", generator=gen).to(torch.bfloat16) for h in range(world)]
+    shards = [shard_experts(gate, up, down, experts, inter, hidden, d, world) for d in range(world)]
+    ops = CudaEpOps()
+    rec = ops.record_bytes(hidden)
+    home = []
+    for h in range(world):
+        routes = ops.route(ls[h], topk)
+        codes, scales = ops.pack_tokens(xs[h])
+        counts, slots = ops.plan(routes, topk, experts, world)
+        sc = counts.tolist()
+        send = ops.pack_records(codes, scales, routes, topk, slots, sum(sc), hidden)
+        home.append((routes, slots, sc, send))
+    # first all-to-all: destination d receives, from every source in rank order, its slice
+    products = []
+    for d in range(world):
+        parts, rc = [], []
+        for h in range(world):
+            sc = home[h][2]
+            lo = sum(sc[:d]) * rec
+            parts.append(home[h][3][lo:lo + sc[d] * rec])
+            rc.append(sc[d])
+        recv = torch.cat(parts) if sum(rc) else torch.empty(rec, dtype=torch.uint8, device="cuda")
+        products.append((ops.experts(recv, sum(rc), hidden, shards[d]), rc))
+    # second all-to-all: home h gets, from every destination in rank order, its products
+    for h in range(world):
+        routes, slots, sc, _ = home[h]
+        back = torch.cat([products[d][0][sum(products[d][1][:h]):sum(products[d][1][:h]) + sc[d]]
+                          for d in range(world)])
+        out = ops.combine(back, slots, routes, topk, hidden)
+        ref_routes = torch.empty(xs[h].shape[0], 2 * topk, dtype=torch.float32, device="cuda")
+        ref = cq.omni_moe(xs[h], ls[h], gate, up, down, experts=experts, topk=topk, routes_out=ref_routes)
+        assert torch.equal(routes, ref_routes)
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), (
+            f"home {h}: {(out.view(torch.int16) != ref.view(torch.int16)).sum().item()} mismatches")
+
+
+# ---------------------------------------------------------------------------------------
+# GPU, 2 processes over NCCL
+# ---------------------------------------------------------------------------------------
+def _nccl_worker(rank, world, port):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
+    import clefq as cq
+    from clefq.ep import omni_moe_ep, shard_experts
+    torch.cuda.set_device(rank)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        experts, topk, hidden, inter, tokens = 32, 8, 512, 256, 257 + 31 * rank
+        gate, up, down = _weights(cq, experts, inter, hidden, 5)
+        shard = shard_experts(gate, up, down, experts, inter, hidden, rank, world)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(1000 + rank)
+        x = torch.randn(tokens, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+        logits = torch.randn(tokens, experts, device="cuda", generator=gen).to(torch.bfloat16)
+        out, routes = omni_moe_ep(x, logits, shard, topk)
+        ref = cq.omni_moe(x, logits, gate, up, down, experts=experts, topk=topk)
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_ep_two_ranks_nccl():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_nccl_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
