@@ -354,6 +354,86 @@ __global__ void combine_kernel(const uint16_t *__restrict__ values, const float 
   }
 }
 
+// Rounds two floats to BF16 with one cvt.rn.bf16x2 and widens them back to F32.
+CQ_DEV void bf16r2_inplace(float &lo, float &hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  lo = __uint_as_float(r << 16);
+  hi = __uint_as_float(r & 0xffff0000u);
+}
+
+// The same combine with topk fixed at compile time: the K route rows' 16-byte chunks are all
+// loaded before the ordered chain consumes them, so a thread has K loads in flight instead
+// of one.  Identical arithmetic and order to combine_kernel.
+template <int K>
+__global__ void combine_k_kernel(const uint16_t *__restrict__ values, const float *__restrict__ routes,
+                                 const float *__restrict__ order, int64_t tokens, int64_t width,
+                                 uint16_t *__restrict__ out) {
+  const int64_t per_tok = width / 8;
+  const int64_t total = tokens * per_tok;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / per_tok;
+    const int64_t c = (i % per_tok) * 8;
+    const float *rt = routes + t * 2 * K;
+    int rank[K];
+    if (order) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        const int r = (int)order[t * K + j];
+        rank[j] = r < 0 ? 0 : (r >= K ? K - 1 : r);
+      }
+    } else {
+      float prev = -1.0f;
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        float best = 1000000.0f;
+        int r = 0;
+#pragma unroll
+        for (int q = 0; q < K; ++q) {
+          const float e = rt[q];
+          if (e > prev && e < best) {
+            best = e;
+            r = q;
+          }
+        }
+        prev = best;
+        rank[j] = r;
+      }
+    }
+    uint4 raw[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) raw[j] = *reinterpret_cast<const uint4 *>(values + (t * K + rank[j]) * width + c);
+    // s = bf16(s + bf16(v * p)) with both roundings done two lanes at a time by
+    // cvt.rn.bf16x2 (round to nearest even, as f32_to_bf16 for every finite value and
+    // for infinities; a NaN stays a NaN).
+    float s[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s[q] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const float p = rt[K + rank[j]];
+      const uint32_t *hw = reinterpret_cast<const uint32_t *>(&raw[j]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float lo = __fmul_rn(__uint_as_float(hw[q] << 16), p);
+        float hi = __fmul_rn(__uint_as_float(hw[q] & 0xffff0000u), p);
+        bf16r2_inplace(lo, hi);
+        lo = __fadd_rn(s[2 * q], lo);
+        hi = __fadd_rn(s[2 * q + 1], hi);
+        bf16r2_inplace(lo, hi);
+        s[2 * q] = lo;
+        s[2 * q + 1] = hi;
+      }
+    }
+    uint4 o;
+    uint32_t *ow = reinterpret_cast<uint32_t *>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)  // the sums are BF16 values already: keep their top halves
+      ow[q] = __byte_perm(__float_as_uint(s[2 * q]), __float_as_uint(s[2 * q + 1]), 0x7632);
+    *reinterpret_cast<uint4 *>(out + t * width + c) = o;
+  }
+}
+
 int launch_combine(const uint16_t *values, const float *routes, const float *order, int64_t tokens, int topk,
                    int64_t width, uint16_t *out, cudaStream_t stream, int num_sms) {
   if (width % 8) return CLEFQ_ERR_SHAPE;
@@ -361,8 +441,13 @@ int launch_combine(const uint16_t *values, const float *routes, const float *ord
   const int64_t total = tokens * (width / 8);
   if (total == 0) return 0;
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
-  combine_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(values, routes, order, tokens, topk,
-                                                                              width, out);
+  const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
+  switch (topk) {
+    case 8: combine_k_kernel<8><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out); break;
+    case 4: combine_k_kernel<4><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out); break;
+    case 2: combine_k_kernel<2><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out); break;
+    default: combine_kernel<<<grid, 256, 0, stream>>>(values, routes, order, tokens, topk, width, out); break;
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
 }
 

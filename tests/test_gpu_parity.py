@@ -338,6 +338,23 @@ def test_combine(cq, ordered, tokens):
     assert np.array_equal(from_dev_bf16(out), ref)
 
 
+@pytest.mark.parametrize("ordered", [True, False])
+@pytest.mark.parametrize("topk", [4, 3, 2])
+def test_combine_other_topk(cq, ordered, topk):
+    """Combine with topk other than 8 (compile-time specialisations for 4 and 2, the generic
+    kernel for 3): distinct random experts per token, bit-exact."""
+    rng = np.random.default_rng(topk)
+    tokens, width, experts = 129, 512, 64
+    ids = np.stack([rng.choice(experts, topk, replace=False) for _ in range(tokens)]).astype(np.float32)
+    probs = o.bf16_to_f32(o.f32_to_bf16(rng.random((tokens, topk)).astype(np.float32)))
+    routes = np.concatenate([ids, probs], axis=1).astype(np.float32)
+    values = bf16_normal(rng, (tokens * topk, width))
+    _, order = o.group(routes, experts)
+    ref = o.combine(values, routes, order if ordered else None)
+    out = cq.omni_combine_ordered(to_dev_bf16(values), to_dev(routes), to_dev(order) if ordered else None)
+    assert np.array_equal(from_dev_bf16(out), ref)
+
+
 @pytest.mark.parametrize("tokens", [300, 1024])
 def test_moe_block(cq, tokens):
     """The fused MoE block (route -> groups -> gate|up -> SwiGLU packing -> down -> combine)
