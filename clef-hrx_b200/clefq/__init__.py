@@ -55,6 +55,10 @@ _SYMBOLS = {
     "clefq_moe_ep_experts": (ctypes.c_int, ["p", "p", "l", "l", "l", "i", "i", "p", "p", "p", "p", "p", "p", "p", "p",
                                             "l"]),
     "clefq_moe_ep_combine": (ctypes.c_int, ["p", "p", "p", "p", "l", "i", "l", "p"]),
+    "clefq_prepare_rowmax": (ctypes.c_int, ["p", "i", "p", "l", "p", "l", "l", "l", "p"]),
+    "clefq_prepare_scaled": (ctypes.c_int, ["p", "i", "i", "p", "l", "p", "l", "l", "l", "l", "p", "p", "p", "l"]),
+    "clefq_tp_gather_unpack": (ctypes.c_int, ["p", "p", "i", "l", "l", "p", "l"]),
+    "clefq_tp_interleave": (ctypes.c_int, ["p", "p", "i", "l", "l", "p", "l"]),
 }
 _CT = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64}
 

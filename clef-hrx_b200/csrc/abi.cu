@@ -22,6 +22,10 @@ int launch_gather_unpack_i4(const uint32_t *a, int64_t a_ld, const int *perm, in
                             uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms);
 int launch_combine(const uint16_t *values, const float *routes, const float *order, int64_t tokens, int topk,
                    int64_t width, uint16_t *out, cudaStream_t stream, int num_sms);
+int launch_tp_gather_unpack(const uint32_t *codes, int world, int64_t rows, int shard_words, uint8_t *op,
+                            int64_t op_ld, cudaStream_t stream, int num_sms);
+int launch_tp_interleave(const uint8_t *src, int world, int64_t rows, int64_t shard_bytes, uint8_t *dst,
+                         int64_t dst_ld, cudaStream_t stream, int num_sms);
 int launch_ep_plan(const float *routes, int64_t tokens, int topk, int experts, int world, long long *counts,
                    int *slots, cudaStream_t stream, int num_sms);
 int launch_ep_pack(const uint32_t *xq, int64_t words_ld, const float *scales, const float *routes, const int *slots,
@@ -122,10 +126,12 @@ static int check_prepare(int kind, int bits, int64_t rows, int64_t width, int64_
 
 static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_t x_ld, const void *aux,
                        int64_t aux_ld, int64_t rows, int64_t width, int64_t stride, void *out, void *operand,
-                       int64_t operand_ld, void *norm_out, int64_t norm_ld) {
+                       int64_t operand_ld, void *norm_out, int64_t norm_ld, float *rowmax_out = nullptr,
+                       const float *rowmax_in = nullptr) {
   int rc = check_prepare(kind, bits, rows, width, stride);
   if (rc) return rc;
-  if (!x || !out || (kind != CLEFQ_PREP_PLAIN && !aux) || (kind == CLEFQ_PREP_NORM_STORE && !norm_out))
+  if (!x || (!out && !rowmax_out) || (kind != CLEFQ_PREP_PLAIN && !aux) ||
+      (kind == CLEFQ_PREP_NORM_STORE && !norm_out))
     return set_err(CLEFQ_ERR_SHAPE, "packing input count");
   if (x_ld < width || !al16(x) || (x_ld * 2) % 16) return set_err(CLEFQ_ERR_ALIGN, "x must be 16-byte aligned rows");
   if (kind == CLEFQ_PREP_SWIGLU && (aux_ld < width || !al16(aux) || (aux_ld * 2) % 16))
@@ -157,6 +163,8 @@ static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_
   a.op_ld = operand_ld;
   a.norm_out = static_cast<uint16_t *>(norm_out);
   a.norm_ld = norm_ld;
+  a.rowmax_out = rowmax_out;
+  a.rowmax_in = rowmax_in;
   return launch_prepare(a, s);  // sets clefq_last_error() itself on failure
 }
 
@@ -234,6 +242,28 @@ int clefq_prepare(void *stream, int kind, int bits, const void *x, int64_t x_ld,
                   void *norm_out, int64_t norm_ld) {
   return run_prepare(static_cast<cudaStream_t>(stream), kind, bits, x, x_ld, aux, aux_ld, rows, width, stride, out,
                      operand, operand_ld, norm_out, norm_ld);
+}
+
+// Split packing of rows sharded by columns over several GPUs (no reference counterpart):
+// each shard publishes its row maxima, the host reduces them with MAX, and every shard then
+// quantises with the full row's maximum, so the codes and scales equal one-GPU packing.
+int clefq_prepare_rowmax(void *stream, int kind, const void *x, int64_t x_ld, const void *aux, int64_t aux_ld,
+                         int64_t rows, int64_t width, float *rowmax) {
+  if (kind != CLEFQ_PREP_PLAIN && kind != CLEFQ_PREP_SWIGLU)
+    return set_err(CLEFQ_ERR_SHAPE, "split packing supports plain and SwiGLU rows");
+  if (!rowmax) return set_err(CLEFQ_ERR_SHAPE, "null row maxima");
+  return run_prepare(static_cast<cudaStream_t>(stream), kind, 4, x, x_ld, aux, aux_ld, rows, width, width, nullptr,
+                     nullptr, 0, nullptr, 0, rowmax, nullptr);
+}
+
+int clefq_prepare_scaled(void *stream, int kind, int bits, const void *x, int64_t x_ld, const void *aux,
+                         int64_t aux_ld, int64_t rows, int64_t width, int64_t stride, const float *rowmax, void *out,
+                         void *operand, int64_t operand_ld) {
+  if (kind != CLEFQ_PREP_PLAIN && kind != CLEFQ_PREP_SWIGLU)
+    return set_err(CLEFQ_ERR_SHAPE, "split packing supports plain and SwiGLU rows");
+  if (!rowmax) return set_err(CLEFQ_ERR_SHAPE, "null row maxima");
+  return run_prepare(static_cast<cudaStream_t>(stream), kind, bits, x, x_ld, aux, aux_ld, rows, width, stride, out,
+                     operand, operand_ld, nullptr, 0, nullptr, rowmax);
 }
 
 int clefq_retile(void *stream, const void *codes, int64_t rows, int64_t cols, int bits, int64_t in_words, void *out) {
@@ -707,6 +737,33 @@ int clefq_moe_ep_combine(void *stream, const void *products, const int32_t *send
   rc = launch_ep_combine(static_cast<const uint16_t *>(products), send_slots, routes, tokens, topk, hidden,
                          static_cast<uint16_t *>(out), static_cast<cudaStream_t>(stream), device_sms());
   return rc ? cuda_err("expert-parallel combine launch") : 0;
+}
+
+// ---- tensor-parallel dense MLP --------------------------------------------------------
+// No reference counterpart (the reference runs the MLP block on one GPU): the data movement
+// after the all-gathers of a host that shards the intermediate dimension over `world` ranks.
+int clefq_tp_gather_unpack(void *stream, const void *codes, int world, int64_t rows, int64_t shard_width,
+                           void *operand, int64_t operand_ld) {
+  if (world < 1 || world > 64 || rows < 0 || shard_width < 256 || shard_width % 256)
+    return set_err(CLEFQ_ERR_SHAPE, "shards must be whole 256-code groups");
+  if (operand_ld < world * shard_width || operand_ld % 16 || !al16(codes) || !al16(operand))
+    return set_err(CLEFQ_ERR_ALIGN, "codes and operand must be 16-byte aligned rows");
+  const int rc = launch_tp_gather_unpack(static_cast<const uint32_t *>(codes), world, rows, (int)(shard_width / 8),
+                                         static_cast<uint8_t *>(operand), operand_ld,
+                                         static_cast<cudaStream_t>(stream), device_sms());
+  return rc ? cuda_err("tensor-parallel unpack launch") : 0;
+}
+
+int clefq_tp_interleave(void *stream, const void *src, int world, int64_t rows, int64_t shard_bytes, void *dst,
+                        int64_t dst_ld_bytes) {
+  if (world < 1 || world > 64 || rows < 0 || shard_bytes <= 0 || shard_bytes % 16)
+    return set_err(CLEFQ_ERR_SHAPE, "shard rows must be a multiple of 16 bytes");
+  if (dst_ld_bytes < world * shard_bytes || dst_ld_bytes % 16 || !al16(src) || !al16(dst))
+    return set_err(CLEFQ_ERR_ALIGN, "source and destination must be 16-byte aligned rows");
+  const int rc = launch_tp_interleave(static_cast<const uint8_t *>(src), world, rows, shard_bytes,
+                                      static_cast<uint8_t *>(dst), dst_ld_bytes, static_cast<cudaStream_t>(stream),
+                                      device_sms());
+  return rc ? cuda_err("tensor-parallel interleave launch") : 0;
 }
 
 }  // extern "C"

@@ -25,6 +25,8 @@ struct PrepareArgs {
   int team_warps;       // warps per row (set by launch_prepare)
   int rows_per_block;
   int stages;           // cp.async stages per thread (GEMM-input packing kernel)
+  float *rowmax_out;    // if set: write each row's |Hadamard| maximum (NaN/inf -> +inf) only
+  const float *rowmax_in;  // if set: quantise with this row maximum instead of the row's own
 };
 int launch_prepare(const PrepareArgs &a, cudaStream_t stream);
 int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);

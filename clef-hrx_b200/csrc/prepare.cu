@@ -360,6 +360,13 @@ __global__ void __launch_bounds__(512, min_blocks_for(CH, KIND)) prepare_kernel(
     for (int off = 8; off >= 1; off >>= 1) rmax = maxnum(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
     rmax = __shfl_sync(0xffffffffu, rmax, 0);
     if (!row_ok) continue;
+    // split packing of a row sharded over several GPUs: publish this shard's maximum, or
+    // quantise with the maximum over all shards
+    if (p.rowmax_out) {
+      if (tid_team == 0) p.rowmax_out[row] = rmax;
+      continue;
+    }
+    if (p.rowmax_in) rmax = p.rowmax_in[row];
 
     const float scale = __fdiv_rn(maxnum(__fmul_rn(rmax, 0.0625f), 1e-30f), qmax);
     const float inv = __fdiv_rn(0.0625f, scale);
@@ -566,6 +573,11 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
     for (int off = 8; off >= 1; off >>= 1) rmax = maxnum(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
     rmax = __shfl_sync(0xffffffffu, rmax, 0);
     if (!row_ok) continue;
+    if (p.rowmax_out) {
+      if (tid_team == 0) p.rowmax_out[row] = rmax;
+      continue;
+    }
+    if (p.rowmax_in) rmax = p.rowmax_in[row];
 
     const float scale = __fdiv_rn(maxnum(__fmul_rn(rmax, 0.0625f), 1e-30f), 7.0f);
     const float inv = __fdiv_rn(0.0625f, scale);
@@ -711,7 +723,8 @@ int launch_prepare(const PrepareArgs &a0, cudaStream_t stream) {
   const int ngroups = a.width >> 8;
   const bool norm = a.mode == MODE_NORM || a.mode == MODE_NORM_STORE;
   if (a.rows == 0) return 0;
-  const bool gemm_input = a.bits == 4 && a.op8 != nullptr && ((uintptr_t)a.out & 15) == 0 &&
+  const bool gemm_input = a.bits == 4 && (a.op8 != nullptr || a.rowmax_out != nullptr) &&
+                          ((uintptr_t)a.out & 15) == 0 &&
                           (a.x_ld & 7) == 0 && (a.mode != MODE_SWIGLU || (a.aux_ld & 7) == 0);
   // The table pays for its 128 KB shared-memory fill once a launch has about a full
   // wave of groups to process; small launches evaluate the activation directly.

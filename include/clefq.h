@@ -252,6 +252,34 @@ CLEFQ_API int clefq_moe_ep_experts(void *stream, const void *records, int64_t n,
 CLEFQ_API int clefq_moe_ep_combine(void *stream, const void *products, const int32_t *send_slots, const float *routes,
                                    int64_t tokens, int topk, int64_t hidden, void *out);
 
+/*
+ * Split packing and tensor-parallel MLP helpers.  No counterpart in the reference, which runs
+ * the MLP block on one GPU (src/backbone.rs:880-894); these serve a host that shards the
+ * intermediate dimension over `world` ranks (rank r: gate/up rows [r*I/G, (r+1)*I/G), down rows
+ * [r*H/G, (r+1)*H/G)).  Per MLP block, on every rank:
+ *   1. clefq_prepare(x) (replicated) and the gate|up GEMM of the rank's intermediate rows
+ *   2. clefq_prepare_rowmax(SwiGLU shard) -> f32 [rows]; all-reduce MAX over the ranks
+ *   3. clefq_prepare_scaled(SwiGLU shard, the reduced maxima) -> int4 codes of the shard,
+ *      with the scales of the full row (identical on every rank)
+ *   4. all-gather the code shards; clefq_tp_gather_unpack -> the full s8 operand
+ *   5. the down GEMM of the rank's output rows; all-gather; clefq_tp_interleave -> [rows][H]
+ * The result is bit-identical to clefq_mlp on one GPU.
+ */
+/* kind: CLEFQ_PREP_PLAIN or CLEFQ_PREP_SWIGLU; rowmax f32 [rows]: max |Hadamard| of the row,
+ * non-finite rows +inf */
+CLEFQ_API int clefq_prepare_rowmax(void *stream, int kind, const void *x, int64_t x_ld, const void *aux,
+                                   int64_t aux_ld, int64_t rows, int64_t width, float *rowmax);
+/* as clefq_prepare (no norm output), with the row scale taken from rowmax[row] */
+CLEFQ_API int clefq_prepare_scaled(void *stream, int kind, int bits, const void *x, int64_t x_ld, const void *aux,
+                                   int64_t aux_ld, int64_t rows, int64_t width, int64_t stride, const float *rowmax,
+                                   void *out, void *operand, int64_t operand_ld);
+/* codes u32 [world][rows][shard_width/8] -> s8 operand [rows][operand_ld] (world*shard_width used) */
+CLEFQ_API int clefq_tp_gather_unpack(void *stream, const void *codes, int world, int64_t rows, int64_t shard_width,
+                                     void *operand, int64_t operand_ld);
+/* src [world][rows][shard_bytes] -> dst [rows][dst_ld_bytes]: rank shards side by side */
+CLEFQ_API int clefq_tp_interleave(void *stream, const void *src, int world, int64_t rows, int64_t shard_bytes,
+                                  void *dst, int64_t dst_ld_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,167 @@
+"""Tensor-parallel dense MLP: the output equals the single-GPU block bit for bit.
+
+- CPU, 2 gloo ranks: the real host orchestration (clefq.tp.mlp_tp) with oracle/numpy
+  stand-ins for the device steps, against the oracle's mlp_block.
+- GPU: the split packing entry points against clefq_prepare; G = 2 and 4 ranks simulated in
+  one process (all-reduce and all-gathers done by hand) through every entry point, against
+  clefq.mlp; 2 processes over NCCL (needs two GPUs).
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+# ---------------------------------------------------------------------------------------
+# CPU: 2 gloo ranks
+# ---------------------------------------------------------------------------------------
+T_M, T_H, T_I = 33, 512, 1024
+
+
+def _cpu_problem():
+    from oracle import oracle as o
+    rng = np.random.default_rng(3)
+    x = o.f32_to_bf16(rng.standard_normal((T_M, T_H)).astype(np.float32))
+    x[5, 17] = 0x7FC0    # a NaN row: zero codes, infinite scale, as on one GPU
+    gate = o.pack_weight(o.f32_to_bf16(rng.standard_normal((T_I, T_H)).astype(np.float32) * 0.05))
+    up = o.pack_weight(o.f32_to_bf16(rng.standard_normal((T_I, T_H)).astype(np.float32) * 0.05))
+    down = o.pack_weight(o.f32_to_bf16(rng.standard_normal((T_H, T_I)).astype(np.float32) * 0.05))
+    return x, gate, up, down
+
+
+def _cpu_worker(rank, world, port):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
+    from oracle import oracle as o
+    from clefq.tp import MlpShard, mlp_tp
+    from tests.tp_oracle_ops import OracleTpOps
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        x, gate, up, down = _cpu_problem()
+
+        def cut(w, rows, cols):
+            per = rows // world
+            words = cols // 8
+            return (w[0][rank * per * words:(rank + 1) * per * words], w[1][rank * per:(rank + 1) * per])
+        shard = MlpShard(cut(gate, T_I, T_H), cut(up, T_I, T_H), cut(down, T_H, T_I), rank, world, T_H, T_I)
+        xt = torch.from_numpy(x.view(np.int16).copy()).view(torch.bfloat16)
+        out = mlp_tp(xt, shard, ops=OracleTpOps())
+        ref = o.mlp_block(x, (gate[0], gate[1], T_I), (up[0], up[1], T_I), (down[0], down[1], T_H))
+        got = out.view(torch.int16).numpy().view(np.uint16)
+        bad = np.count_nonzero(got != ref)
+        assert bad == 0, f"rank {rank}: {bad} mismatches"
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_host_logic_two_gloo_ranks():
+    mp.start_processes(_cpu_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
+
+
+# ---------------------------------------------------------------------------------------
+# GPU
+# ---------------------------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def cq():
+    import clefq
+    clefq.lib()
+    return clefq
+
+
+def _weights(cq, hidden, inter, seed):
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+
+    def w(rows, cols):
+        return cq.load_quantized_weight((torch.randn(rows, cols, device="cuda", generator=gen) * 0.05)
+                                        .to(torch.bfloat16))
+    return w(inter, hidden), w(inter, hidden), w(hidden, inter)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,width", [(7, 768), (300, 4096), (1000, 3072)])
+def test_split_packing_matches_prepare(cq, rows, width):
+    """rowmax + scaled packing of a whole row == clefq_prepare (codes, scales, operand)."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(rows)
+    gu = (torch.randn(rows, 2 * width, device="cuda", generator=gen) * 2).to(torch.bfloat16)
+    gu[3 % rows, 5] = float("nan")
+    from clefq.tp import CudaTpOps
+    ops = CudaTpOps()
+    ref = cq.prepare(gu[:, :width], 4, width, cq.PREP_SWIGLU, gu[:, width:])
+    mx = ops.rowmax(gu)
+    codes, scales = ops.pack_hidden(gu, mx)
+    assert torch.equal(codes, ref.codes)
+    assert torch.equal(scales.view(torch.int32), ref.scales.view(torch.int32))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,m,residual", [(2, 300, False), (4, 129, True), (2, 2048, True)])
+def test_tp_simulated_ranks_match_single_gpu(cq, world, m, residual):
+    from clefq.tp import CudaTpOps, shard_mlp
+    hidden, inter = 1024, 4096
+    gate, up, down = _weights(cq, hidden, inter, 21)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(m)
+    x = torch.randn(m, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+    res = torch.randn(m, hidden, device="cuda", generator=gen).to(torch.bfloat16) if residual else None
+    shards = [shard_mlp(gate, up, down, r, world) for r in range(world)]
+    ops = CudaTpOps()
+    gus = [ops.gate_up(ops.pack_x(x), m, s) for s in shards]
+    mx = torch.stack([ops.rowmax(g) for g in gus]).amax(dim=0)      # all-reduce(MAX)
+    packed = [ops.pack_hidden(g, mx) for g in gus]
+    for _, sc in packed[1:]:
+        assert torch.equal(sc, packed[0][1])                           # same scales on every rank
+    codes_all = torch.stack([c for c, _ in packed])                   # all-gather
+    operand = ops.gather_unpack(codes_all, inter)
+    parts = [ops.down(operand, packed[r][1], shards[r], res) for r in range(world)]
+    out = ops.interleave(torch.stack(parts))                          # all-gather + interleave
+    ref = cq.mlp(x, gate, up, down, residual=res)
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), (
+        f"{(out.view(torch.int16) != ref.view(torch.int16)).sum().item()} mismatches")
+
+
+def _nccl_worker(rank, world, port):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
+    import clefq as cq
+    from clefq.tp import mlp_tp, shard_mlp
+    torch.cuda.set_device(rank)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        hidden, inter, m = 2048, 8192, 777
+        gate, up, down = _weights(cq, hidden, inter, 9)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(5)                       # the same input on every rank
+        x = torch.randn(m, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+        res = torch.randn(m, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+        out = mlp_tp(x, shard_mlp(gate, up, down, rank, world), residual=res)
+        ref = cq.mlp(x, gate, up, down, residual=res)
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_tp_two_ranks_nccl():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_nccl_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
