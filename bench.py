@@ -344,6 +344,42 @@ def run_clefq(args, world, rank, local):
                else "single GPU", "tokens_per_s": world * MOE_T / (mms / 1000), "ms_per_step": mms,
                "tops": ops / (mms / 1000) / 1e12, "frac_of_int8_peak": ops / (mms / 1000) / 1e12 / i8_peak}
 
+    # ---- tensor-parallel C2 block (N > 1): one 4096-token block shared by all ranks -------
+    tp = None
+    if world > 1 and not args.skip_tp:
+        from clefq.tp import MlpShard, TpComm, mlp_tp, mlp_tp_fused, tp_mlp_region_bytes
+        tgen = torch.Generator(device="cuda")
+        tgen.manual_seed(77)                    # the same input on every rank
+        tx = torch.randn(M, HIDDEN, device="cuda", generator=tgen).to(torch.bfloat16)
+        tshard = MlpShard(rand_weight_dev(clefq, INTER // world, HIDDEN, gen),
+                          rand_weight_dev(clefq, INTER // world, HIDDEN, gen),
+                          rand_weight_dev(clefq, HIDDEN // world, INTER, gen), rank, world, HIDDEN, INTER)
+        comm = TpComm(tp_mlp_region_bytes(M, HIDDEN, INTER, world))
+        tws = torch.empty(clefq.lib().clefq_tp_mlp_workspace_size(M, HIDDEN, INTER, world), dtype=torch.uint8,
+                          device="cuda")
+        tout = torch.empty((M, HIDDEN), dtype=torch.bfloat16, device="cuda")
+
+        def timed(step):
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            clefq.status()
+            barrier(world)
+            tt = time_steps(step, max(5, min(args.steps, 30)), flush)
+            clefq.status()
+            return all_max(world, sum(tt) / len(tt))
+        fms = timed(lambda: mlp_tp_fused(tx, tshard, comm, workspace=tws, out=tout))
+        nms = timed(lambda: mlp_tp(tx, tshard))
+        barrier(world)
+        comm.close()
+        tp = {"workload": "C2 dense INT4 SwiGLU MLP block, 4096 tokens shared by all ranks",
+              "parallelism": f"tp{world}: intermediate sharded; one clefq_tp_mlp call whose packing kernel and "
+                             "down-GEMM epilogue store their shards into every rank's buffer over NVLink, with "
+                             "device barriers", "scaling": "strong",
+              "tokens_per_s": M / (fms / 1000), "ms_per_step": fms,
+              "nccl_collectives_ms_per_step": nms,
+              "gpu_launches_per_step": 8}
+
     launches = 4 * args.steps
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -366,6 +402,8 @@ def run_clefq(args, world, rank, local):
     }
     if moe:
         line["secondary"] = moe
+    if tp:
+        line["tensor_parallel"] = tp
     if rank == 0 and world == 1 and not args.skip_cpu:
         threads = len(os.sched_getaffinity(0))
         cpu_val, reps, el = cpu_mlp_sample(512, 10.0, threads)
@@ -383,6 +421,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="clefq", choices=["clefq", "reference"])
     ap.add_argument("--skip-moe", action="store_true")
+    ap.add_argument("--skip-tp", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -59,6 +59,20 @@ _SYMBOLS = {
     "clefq_prepare_scaled": (ctypes.c_int, ["p", "i", "i", "p", "l", "p", "l", "l", "l", "l", "p", "p", "p", "l"]),
     "clefq_tp_gather_unpack": (ctypes.c_int, ["p", "p", "i", "l", "l", "p", "l"]),
     "clefq_tp_interleave": (ctypes.c_int, ["p", "p", "i", "l", "l", "p", "l"]),
+    "clefq_comm_handle_bytes": (ctypes.c_int64, []),
+    "clefq_comm_create": (ctypes.c_int, ["i", "i", "l", "p", "p"]),
+    "clefq_comm_open": (ctypes.c_int, ["p", "p"]),
+    "clefq_comm_attach": (ctypes.c_int, ["p", "i", "p"]),
+    "clefq_comm_ready": (ctypes.c_int, ["p"]),
+    "clefq_comm_region": (ctypes.c_void_p, ["p"]),
+    "clefq_comm_region_bytes": (ctypes.c_int64, ["p"]),
+    "clefq_comm_set_timeout_ms": (ctypes.c_int, ["p", "l"]),
+    "clefq_comm_barrier": (ctypes.c_int, ["p", "p"]),
+    "clefq_comm_destroy": (ctypes.c_int, ["p"]),
+    "clefq_tp_mlp_region_bytes": (ctypes.c_int64, ["l", "l", "l", "i"]),
+    "clefq_tp_mlp_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i"]),
+    "clefq_tp_mlp": (ctypes.c_int, ["p", "p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "p", "l"]),
+    "clefq_tp_mlp_output": (ctypes.c_void_p, ["p", "l", "l", "l"]),
 }
 _CT = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64}
 

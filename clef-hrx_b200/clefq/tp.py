@@ -12,9 +12,15 @@ GPU.  Here the intermediate dimension I is split over G ranks: rank r owns gate/
 Hadamard groups never straddle a shard, the row scale comes from the whole row and every
 output column of down sees the full K, so the output equals `clefq.mlp` bit for bit.  The
 exchanged bytes per block are M*I/2 (packed codes), M*H*2 (output) and M*4 (maxima).
+
+`mlp_tp` runs these steps as separate kernels and torch.distributed collectives (any
+backend; the CPU tests drive it over gloo).  `mlp_tp_fused` is the B200 path: one C-ABI call
+(clefq_tp_mlp) over a `TpComm`, whose packing kernel and GEMM epilogue store their shards
+straight into every rank's symmetric buffer over NVLink, ordered by device barriers.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -147,3 +153,93 @@ def mlp_tp(x: torch.Tensor, shard: MlpShard, residual=None, group=None, ops=None
     out_all = torch.empty((world,) + tuple(part.shape), dtype=part.dtype, device=part.device)
     _all_gather(out_all, part, group)
     return ops.interleave(out_all)
+
+
+class TpComm:
+    """This rank's symmetric region, mapped into every rank of `group` (clefq_comm_*).
+
+    Collective: every rank constructs it with the same `region_bytes` (at least
+    `tp_mlp_region_bytes` of the largest block it will run).  Without an initialised process
+    group it is a one-rank communicator."""
+
+    def __init__(self, region_bytes: int, group=None, timeout_ms: int | None = None):
+        from . import _call, lib
+        distributed = dist.is_available() and dist.is_initialized()
+        self.rank = dist.get_rank(group) if distributed else 0
+        self.world = dist.get_world_size(group) if distributed else 1
+        self.region_bytes = int(region_bytes)
+        hb = lib().clefq_comm_handle_bytes()
+        handle = ctypes.create_string_buffer(hb)
+        self._comm = ctypes.c_void_p()
+        _call("clefq_comm_create", self.rank, self.world, self.region_bytes, ctypes.byref(self._comm), handle)
+        if self.world > 1:
+            dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" else "cpu"
+            mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(dev)
+            every = torch.empty((self.world, hb), dtype=torch.uint8, device=dev)
+            _all_gather(every, mine, group)
+            _call("clefq_comm_open", self._comm, ctypes.create_string_buffer(every.cpu().numpy().tobytes()))
+        if timeout_ms:
+            _call("clefq_comm_set_timeout_ms", self._comm, int(timeout_ms))
+        if self.world > 1:
+            dist.barrier(group)
+
+    @property
+    def handle(self):
+        if self._comm is None:
+            raise RuntimeError("TpComm is closed")
+        return self._comm
+
+    def barrier(self):
+        from . import _call, _stream
+        _call("clefq_comm_barrier", self.handle, _stream())
+
+    def close(self):
+        """Releases the region (after the device is done with it); not collective."""
+        from . import _call
+        if self._comm is not None:
+            torch.cuda.synchronize()
+            _call("clefq_comm_destroy", self._comm)
+            self._comm = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+def tp_mlp_region_bytes(m: int, hidden: int, inter: int, world: int) -> int:
+    from . import lib
+    n = lib().clefq_tp_mlp_region_bytes(m, hidden, inter, world)
+    if n < 0:
+        raise ValueError("unsupported tensor-parallel MLP shape")
+    return n
+
+
+def mlp_tp_fused(x: torch.Tensor, shard: MlpShard, comm: TpComm, residual=None, workspace=None, out=None):
+    """Tensor-parallel MLP block in one C-ABI call (clefq_tp_mlp); every rank passes the same
+    x (and residual) and gets the whole output [M][H], bit-identical to `clefq.mlp`."""
+    from . import _call, _need_cuda, _ptr, _stream, lib
+    _need_cuda(x, residual)
+    if shard.world != comm.world or shard.rank != comm.rank:
+        raise ValueError("MLP shard does not match the communicator")
+    m, hidden = x.shape
+    if hidden != shard.hidden:
+        raise ValueError("MLP input width does not match the shard")
+    x = x.contiguous()
+    if residual is not None:
+        residual = residual.contiguous()
+        if residual.shape != x.shape:
+            raise ValueError("residual shape must match x")
+    need = lib().clefq_tp_mlp_workspace_size(m, hidden, shard.inter, shard.world)
+    if need < 0:
+        raise ValueError("unsupported tensor-parallel MLP shape")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    if out is None:
+        out = torch.empty((m, hidden), dtype=torch.bfloat16, device=x.device)
+    g, u, d = shard.gate, shard.up, shard.down
+    _call("clefq_tp_mlp", comm.handle, _stream(), _ptr(x), m, hidden, shard.inter, _ptr(g.codes), _ptr(g.scales),
+          _ptr(u.codes), _ptr(u.scales), _ptr(d.codes), _ptr(d.scales), _ptr(residual), _ptr(out), _ptr(workspace),
+          need)
+    return out

@@ -64,25 +64,6 @@ int current_device() {
   return d < 0 || d >= 64 ? 0 : d;
 }
 
-// Bump allocator over a caller workspace (256-byte aligned sections).
-struct Arena {
-  uint8_t *base;
-  int64_t cap, used = 0;
-  bool ok = true;
-  template <class T>
-  T *take(int64_t count) {
-    int64_t off = (used + 255) & ~int64_t(255);
-    int64_t bytes = count * (int64_t)sizeof(T);
-    if (off + bytes > cap) {
-      ok = false;
-      return nullptr;
-    }
-    used = off + bytes;
-    return base ? reinterpret_cast<T *>(base + off) : nullptr;
-  }
-};
-int64_t aligned_total(const Arena &a) { return (a.used + 255) & ~int64_t(255); }
-
 bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 }  // namespace
 
@@ -127,7 +108,8 @@ static int check_prepare(int kind, int bits, int64_t rows, int64_t width, int64_
 static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_t x_ld, const void *aux,
                        int64_t aux_ld, int64_t rows, int64_t width, int64_t stride, void *out, void *operand,
                        int64_t operand_ld, void *norm_out, int64_t norm_ld, float *rowmax_out = nullptr,
-                       const float *rowmax_in = nullptr) {
+                       const float *rowmax_in = nullptr, uint32_t *const *code_dst = nullptr,
+                       int n_code_dst = 0, int64_t code_ld = 0) {
   int rc = check_prepare(kind, bits, rows, width, stride);
   if (rc) return rc;
   if (!x || (!out && !rowmax_out) || (kind != CLEFQ_PREP_PLAIN && !aux) ||
@@ -165,12 +147,16 @@ static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_
   a.norm_ld = norm_ld;
   a.rowmax_out = rowmax_out;
   a.rowmax_in = rowmax_in;
+  for (int d = 0; d < n_code_dst; ++d) a.code_dst[d] = code_dst[d];
+  a.n_code_dst = n_code_dst;
+  a.code_ld = code_ld;
   return launch_prepare(a, s);  // sets clefq_last_error() itself on failure
 }
 
 static int run_gemm(cudaStream_t s, int bits, const uint8_t *op, int64_t op_ld, int64_t op_rows, const float *a_scales,
                     int64_t m, const void *w0, const float *ws0, const void *w1, const float *ws1, int n_split, int64_t n,
-                    int64_t k, const void *residual, int64_t residual_ld, int out_dtype, void *out, int64_t out_ld) {
+                    int64_t k, const void *residual, int64_t residual_ld, int out_dtype, void *out, int64_t out_ld,
+                    uint16_t *const *out_peer = nullptr, int n_out_peer = 0) {
   int *status = device_status_word();
   if (!status) return cuda_err("status word");
   GemmParams p{};
@@ -193,6 +179,8 @@ static int run_gemm(cudaStream_t s, int bits, const uint8_t *op, int64_t op_ld, 
   p.residual = static_cast<const uint16_t *>(residual);
   p.ldr = residual_ld;
   p.err = status;
+  for (int d = 0; d < n_out_peer; ++d) p.out_peer[d] = out_peer[d];
+  p.n_out_peer = n_out_peer;
   int rc = launch_gemm(p, s);
   if (rc == CLEFQ_ERR_CUDA) return cuda_err("gemm launch");
   if (rc) return set_err(rc, "unsupported integer GEMM shape or alignment (n %% 128, k %% 256, 16-byte operand rows)");
@@ -494,6 +482,146 @@ int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t in
   if (rc) return rc;
   return run_gemm(s, 4, h8, inter, m, reinterpret_cast<const float *>(hq + m * (si / 8)), m, down_tiled, down_scales,
                   nullptr, nullptr, (int)(hidden / 128), hidden, inter, residual, hidden, CLEFQ_BF16, out, hidden);
+}
+
+// ---- tensor-parallel MLP block, collectives fused into its kernels --------------------
+// Symmetric region (same offsets on every rank): maxes f32 [world][m] (slot g written by
+// rank g), the int4 hidden codes [m][inter/8] (words [g*I/8G, (g+1)*I/8G) of each row written
+// by rank g's packing kernel) and the output [m][hidden] (columns [g*H/G, (g+1)*H/G) written
+// by rank g's GEMM epilogue).  Codes cross NVLink packed (half the bytes of the s8 operand,
+// in whole 32-byte sectors); each rank unpacks the full operand locally.
+static Arena tp_region(Arena a, int64_t m, int64_t hidden, int64_t inter, int world, float **maxes, uint32_t **codes,
+                       uint16_t **out) {
+  *maxes = a.take<float>(world * m);
+  *codes = a.take<uint32_t>(m * (inter / 8));
+  *out = a.take<uint16_t>(m * hidden);
+  return a;
+}
+
+static Arena tp_tables(Arena a, int64_t m, int64_t hidden, int64_t inter, int64_t shard, uint32_t **xq, uint8_t **x8,
+                       uint16_t **gu, uint32_t **hq, float **mx, uint8_t **h8) {
+  *xq = a.take<uint32_t>(m * (stride_for(hidden) / 8 + 1));
+  *x8 = a.take<uint8_t>(m * hidden);
+  *gu = a.take<uint16_t>(m * 2 * shard);
+  *hq = a.take<uint32_t>(m * (shard / 8 + 1));
+  *mx = a.take<float>(m);
+  *h8 = a.take<uint8_t>(m * inter);
+  return a;
+}
+
+static int check_tp_mlp(int world, int64_t m, int64_t hidden, int64_t inter) {
+  if (world < 1 || world > kMaxRanks || m < 1 || hidden < 256 || inter < 256 || hidden > 32768 || inter > 32768 ||
+      inter % (256 * world) || hidden % (256 * world))
+    return set_err(CLEFQ_ERR_SHAPE,
+                   "unsupported tensor-parallel MLP shape: each rank needs whole 256-groups of the intermediate "
+                   "and a multiple of 256 output columns");
+  return 0;
+}
+
+int64_t clefq_tp_mlp_region_bytes(int64_t m, int64_t hidden, int64_t inter, int world) {
+  if (check_tp_mlp(world, m, hidden, inter)) return -1;
+  float *mx;
+  uint32_t *codes;
+  uint16_t *out;
+  return aligned_total(tp_region(Arena{nullptr, INT64_MAX}, m, hidden, inter, world, &mx, &codes, &out));
+}
+
+int64_t clefq_tp_mlp_workspace_size(int64_t m, int64_t hidden, int64_t inter, int world) {
+  if (check_tp_mlp(world, m, hidden, inter)) return -1;
+  uint32_t *xq, *hq;
+  uint8_t *x8, *h8;
+  uint16_t *gu;
+  float *mx;
+  return aligned_total(
+      tp_tables(Arena{nullptr, INT64_MAX}, m, hidden, inter, inter / world, &xq, &x8, &gu, &hq, &mx, &h8));
+}
+
+int clefq_tp_mlp(clefq_comm *c, void *stream, const void *x, int64_t m, int64_t hidden, int64_t inter,
+                 const void *gate_tiled, const float *gate_scales, const void *up_tiled, const float *up_scales,
+                 const void *down_tiled, const float *down_scales, const void *residual, void *out, void *workspace,
+                 int64_t workspace_bytes) {
+  if (!clefq_comm_ready(c)) return set_err(CLEFQ_ERR_SHAPE, "tensor-parallel MLP: communicator peers not opened");
+  int rc = check_tp_mlp(c->world, m, hidden, inter);
+  if (rc) return rc;
+  if (!x || !out) return set_err(CLEFQ_ERR_SHAPE, "tensor-parallel MLP: null input or output");
+  if (!al16(x) || (residual && !al16(residual))) return set_err(CLEFQ_ERR_ALIGN, "x and residual must be 16-byte aligned");
+  const int world = c->world, rank = c->rank;
+  const int64_t shard = inter / world, cols = hidden / world;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float *maxes;
+  uint32_t *codes;
+  uint16_t *rout;
+  Arena region = tp_region(Arena{c->base + kCommHeader, c->bytes}, m, hidden, inter, world, &maxes, &codes, &rout);
+  if (!region.ok) return set_err(CLEFQ_ERR_WORKSPACE, "communicator region too small for this MLP block");
+  uint32_t *xq, *hq;
+  uint8_t *x8, *h8;
+  uint16_t *gu;
+  float *mx;
+  Arena a = tp_tables(Arena{static_cast<uint8_t *>(workspace), workspace_bytes}, m, hidden, inter, shard, &xq, &x8,
+                      &gu, &hq, &mx, &h8);
+  if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "tensor-parallel MLP workspace too small");
+  int *status = device_status_word();
+  if (!status) return cuda_err("status word");
+  // the same object in rank g's region
+  auto at = [&](int g, const void *p) { return c->peer[g] + (static_cast<const uint8_t *>(p) - c->base); };
+  const int64_t sh = stride_for(hidden);
+  // 1. x packed on every rank; gate|up of this rank's intermediate rows
+  rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, m, hidden, sh, xq, x8, hidden, nullptr, 0);
+  if (rc) return rc;
+  rc = run_gemm(s, 4, x8, hidden, m, reinterpret_cast<const float *>(xq + m * (sh / 8)), m, gate_tiled, gate_scales,
+                up_tiled, up_scales, (int)(shard / 128), 2 * shard, hidden, nullptr, 0, CLEFQ_BF16, gu, 2 * shard);
+  if (rc) return rc;
+  // 2. |Hadamard| row maxima of the SwiGLU shard into this rank's slot; the barrier stores the
+  //    slot into every peer and reduces the slots to the full-row maxima
+  float *slot = maxes + rank * m;
+  rc = run_prepare(s, CLEFQ_PREP_SWIGLU, 4, gu, 2 * shard, gu + shard, 2 * shard, m, shard, shard, nullptr, nullptr,
+                   0, nullptr, 0, slot, nullptr);
+  if (rc) return rc;
+  CommBarrierArgs b = comm_barrier_args(c, status);
+  b.src = reinterpret_cast<const uint32_t *>(slot);
+  for (int g = 0; g < world; ++g) b.dst[g] = reinterpret_cast<uint32_t *>(at(g, slot));
+  b.words = m;
+  b.maxes = maxes;
+  b.mx = mx;
+  b.m = m;
+  if ((rc = launch_comm_barrier(b, s))) return rc;
+  // 3. the shard quantised with the full-row maxima; its code words go into every rank's
+  //    code buffer (this rank's included); after the barrier the full rows are unpacked
+  uint32_t *code_cols = codes + rank * (shard / 8);
+  uint32_t *code_dst[kMaxRanks];
+  uint16_t *out_peer[kMaxPeers];
+  uint16_t *out_cols = rout + rank * cols;
+  int np = 0;
+  for (int g = 0; g < world; ++g) {
+    code_dst[g] = reinterpret_cast<uint32_t *>(at(g, code_cols));
+    if (g != rank) out_peer[np++] = reinterpret_cast<uint16_t *>(at(g, out_cols));
+  }
+  rc = run_prepare(s, CLEFQ_PREP_SWIGLU, 4, gu, 2 * shard, gu + shard, 2 * shard, m, shard, shard, hq, nullptr, 0,
+                   nullptr, 0, nullptr, mx, code_dst, world, inter / 8);
+  if (rc) return rc;
+  if ((rc = launch_comm_barrier(comm_barrier_args(c, status), s))) return rc;
+  if (launch_unpack_i4(codes, inter / 8, m, (int)inter, h8, inter, s, device_sms()))
+    return cuda_err("tensor-parallel MLP operand unpack");
+  // 4. down GEMM of this rank's output columns over the full operand, stored into every
+  //    rank's output buffer
+  const uint16_t *res_cols = residual ? static_cast<const uint16_t *>(residual) + rank * cols : nullptr;
+  rc = run_gemm(s, 4, h8, inter, m, reinterpret_cast<const float *>(hq + m * (shard / 8)), m, down_tiled, down_scales,
+                nullptr, nullptr, (int)(cols / 128), cols, inter, res_cols, hidden, CLEFQ_BF16, out_cols, hidden,
+                out_peer, np);
+  if (rc) return rc;
+  if ((rc = launch_comm_barrier(comm_barrier_args(c, status), s))) return rc;
+  if (out != rout && cudaMemcpyAsync(out, rout, m * hidden * 2, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return cuda_err("tensor-parallel MLP output copy");
+  return 0;
+}
+
+void *clefq_tp_mlp_output(clefq_comm *c, int64_t m, int64_t hidden, int64_t inter) {
+  if (!c || check_tp_mlp(c->world, m, hidden, inter)) return nullptr;
+  float *maxes;
+  uint32_t *codes;
+  uint16_t *rout;
+  Arena region = tp_region(Arena{c->base + kCommHeader, c->bytes}, m, hidden, inter, c->world, &maxes, &codes, &rout);
+  return region.ok ? rout : nullptr;
 }
 
 // ---- grouped expert FFN shared by the fused MoE block and the expert-parallel path ----

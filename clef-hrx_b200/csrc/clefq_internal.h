@@ -7,6 +7,9 @@
 
 namespace cq {
 
+constexpr int kMaxRanks = 8;              // ranks of a tensor-parallel group (one node)
+constexpr int kMaxPeers = kMaxRanks - 1;  // extra store destinations of a fused collective
+
 struct PrepareArgs {
   const uint16_t *x;
   int64_t x_ld;
@@ -27,6 +30,11 @@ struct PrepareArgs {
   int stages;           // cp.async stages per thread (GEMM-input packing kernel)
   float *rowmax_out;    // if set: write each row's |Hadamard| maximum (NaN/inf -> +inf) only
   const float *rowmax_in;  // if set: quantise with this row maximum instead of the row's own
+  // GEMM-input packing only: every code word (row, w) is also stored at
+  // code_dst[d][row * code_ld + w], e.g. into the ranks' symmetric buffers over NVLink
+  uint32_t *code_dst[kMaxRanks];
+  int64_t code_ld;
+  int n_code_dst;
 };
 int launch_prepare(const PrepareArgs &a, cudaStream_t stream);
 int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);
@@ -65,14 +73,70 @@ struct GemmParams {
   int scale_mode;           // a_scales index: 0 -> p, 1 -> perm[p] / topk, 2 -> perm[p]
   int scatter;              // output row: 1 -> perm[p], 0 -> p
   int *err;                 // device status word
+  // dense 2-SM kernel only: every output row is also stored at these bases (same offsets
+  // as from out), e.g. peers' symmetric buffers over NVLink
+  uint16_t *out_peer[kMaxPeers];
+  int n_out_peer;
 };
 int launch_gemm(const GemmParams &p, cudaStream_t stream);
 // Token rows per tile of the kernel launch_gemm picks for this output shape (grouped
 // callers build their tile lists with it).
 int gemm_tile_rows(int n, int n_split);
 
+// Bump allocator over a caller workspace (256-byte aligned sections); with a null base it
+// only measures.
+struct Arena {
+  uint8_t *base;
+  int64_t cap, used = 0;
+  bool ok = true;
+  template <class T>
+  T *take(int64_t count) {
+    int64_t off = (used + 255) & ~int64_t(255);
+    int64_t bytes = count * (int64_t)sizeof(T);
+    if (off + bytes > cap) {
+      ok = false;
+      return nullptr;
+    }
+    used = off + bytes;
+    return base ? reinterpret_cast<T *>(base + off) : nullptr;
+  }
+};
+inline int64_t aligned_total(const Arena &a) { return (a.used + 255) & ~int64_t(255); }
+
+// One rank's view of the symmetric regions of a node-local group (comm.cu).
+constexpr int64_t kCommHeader = 4096;  // flags and the epoch counter precede the caller's bytes
+
+struct CommBarrierArgs {
+  uint32_t *flags;                  // this rank's flags[world]
+  uint32_t *peer_flags[kMaxRanks];  // rank g's flags as mapped here (null for this rank)
+  uint32_t *counter;                // this rank's epoch counter
+  int rank, world;
+  int64_t timeout_ns;
+  const uint32_t *src;              // optional: `words` 4-byte words stored at dst[g] of every peer
+  uint32_t *dst[kMaxRanks];
+  int64_t words;
+  const float *maxes;               // optional, after the wait: mx[i] = max_g maxes[g * m + i]
+  float *mx;
+  int64_t m;
+  int *err;
+};
+int launch_comm_barrier(const CommBarrierArgs &a, cudaStream_t stream);
+
 int device_sms();
 int report_error(int code, const char *msg);  // sets clefq_last_error()
 int *device_status_word();  // per-device zero-initialised status word used by bounded waits
 
+}  // namespace cq
+
+struct clefq_comm {
+  int rank, world, device;
+  int64_t bytes;                      // caller bytes of every region (after the header)
+  uint8_t *base;                      // this rank's region
+  uint8_t *peer[cq::kMaxRanks];       // every rank's region as mapped here (peer[rank] = base)
+  bool opened[cq::kMaxRanks];         // peer[g] was opened from an IPC handle
+  int64_t timeout_ns;                 // bound of each barrier wait
+};
+
+namespace cq {
+CommBarrierArgs comm_barrier_args(clefq_comm *c, int *err);
 }  // namespace cq

@@ -463,6 +463,9 @@ int launch_gemm(const GemmParams &p, cudaStream_t stream) {
   if (p.out && ((uintptr_t)p.out % 8 || p.ldo % 4)) return CLEFQ_ERR_ALIGN;
   if (p.residual && ((uintptr_t)p.residual % 8 || p.ldr % 4)) return CLEFQ_ERR_ALIGN;
   const bool pairs = gemm_uses_pairs(p);
+  if (p.n_out_peer && (!pairs || p.grouped || !p.out || p.n_out_peer > kMaxPeers)) return CLEFQ_ERR_SHAPE;
+  for (int d = 0; d < p.n_out_peer; ++d)
+    if ((uintptr_t)p.out_peer[d] % 8) return CLEFQ_ERR_ALIGN;
   const int tile_rows = pairs ? two_sm::BN2 : BN;
   if (p.grouped && p.tile_rows != tile_rows) return CLEFQ_ERR_SHAPE;  // tile list built for the other kernel
   const int64_t tiles_m = p.grouped ? p.max_tiles : (p.m + tile_rows - 1) / tile_rows;

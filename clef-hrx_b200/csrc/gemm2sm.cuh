@@ -377,7 +377,13 @@ __global__ void __launch_bounds__(THREADS2, 1)
             for (int qq = 0; qq < 4; ++qq) o4[qq] = f32_to_bf16(__fadd_rn(bf16_to_f32(hr[qq]), bf16_to_f32(hv[qq])));
             v = *reinterpret_cast<uint2 *>(o4);
           }
-          *reinterpret_cast<uint2 *>(p.out + orow * p.ldo + col0 + 4 * lane) = v;
+          const int64_t off = orow * p.ldo + col0 + 4 * lane;
+          *reinterpret_cast<uint2 *>(p.out + off) = v;
+          if (!GROUPED && p.n_out_peer) {
+#pragma unroll
+            for (int d = 0; d < kMaxPeers; ++d)
+              if (d < p.n_out_peer) *reinterpret_cast<uint2 *>(p.out_peer[d] + off) = v;
+          }
         }
         named_barrier_sync(1, 32 * EPI_WARPS);
       }

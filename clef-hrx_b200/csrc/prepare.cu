@@ -583,7 +583,6 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
     const float inv = __fdiv_rn(0.0625f, scale);
     const bool finite = scale < __int_as_float(0x7f800000);
     uint32_t *orow = p.out + row * words;
-    uint8_t *oprow = p.op8 + row * p.op_ld;
 #pragma unroll
     for (int sl = 0; sl < NS; ++sl) {
       const int g = gidx[sl];
@@ -600,9 +599,18 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
         // code word g*32 + 8k + r is word (r & 3) of its 32-code operand block: the s8
         // operand holds 16 * code, low nibbles of the block's 4 words first, then high
         orow[g * 32 + 8 * k + r] = w;
-        uint8_t *op = oprow + g * 256 + k * 64 + (r >> 2) * 32 + (r & 3) * 4;
-        *reinterpret_cast<uint32_t *>(op) = nib_lo16(w);
-        *reinterpret_cast<uint32_t *>(op + 16) = nib_hi16(w);
+        if (TAB && p.n_code_dst) {
+          // eight lanes store 32 contiguous bytes: whole sectors, also over NVLink
+          const int64_t cw = row * p.code_ld + g * 32 + 8 * k + r;
+#pragma unroll
+          for (int d = 0; d < kMaxRanks; ++d)
+            if (d < p.n_code_dst) p.code_dst[d][cw] = w;
+        }
+        if (p.op8) {
+          uint8_t *op = p.op8 + row * p.op_ld + g * 256 + k * 64 + (r >> 2) * 32 + (r & 3) * 4;
+          *reinterpret_cast<uint32_t *>(op) = nib_lo16(w);
+          *reinterpret_cast<uint32_t *>(op + 16) = nib_hi16(w);
+        }
       }
     }
     // Stride padding words are zeroed; the scale follows all code rows.
@@ -723,16 +731,21 @@ int launch_prepare(const PrepareArgs &a0, cudaStream_t stream) {
   const int ngroups = a.width >> 8;
   const bool norm = a.mode == MODE_NORM || a.mode == MODE_NORM_STORE;
   if (a.rows == 0) return 0;
-  const bool gemm_input = a.bits == 4 && (a.op8 != nullptr || a.rowmax_out != nullptr) &&
+  const bool gemm_input = a.bits == 4 && (a.op8 != nullptr || a.rowmax_out != nullptr || a.n_code_dst > 0) &&
                           ((uintptr_t)a.out & 15) == 0 &&
                           (a.x_ld & 7) == 0 && (a.mode != MODE_SWIGLU || (a.aux_ld & 7) == 0);
   // The table pays for its 128 KB shared-memory fill once a launch has about a full
   // wave of groups to process; small launches evaluate the activation directly.
-  const bool tab = gemm_input && a.mode == MODE_SWIGLU && a.rows * (int64_t)ngroups >= 2048;
+  // Extra code destinations exist only in the GEMM-input kernel, so they take the table at
+  // any size.
+  const bool tab = gemm_input && a.mode == MODE_SWIGLU && (a.rows * (int64_t)ngroups >= 2048 || a.n_code_dst);
+  if (a.n_code_dst && !tab)
+    return report_error(CLEFQ_ERR_SHAPE, "prepare: extra code destinations are for SwiGLU GEMM-input packing");
   if (gemm_input && (a.mode == MODE_PLAIN || tab) && try_launch_pack(a, tab, stream)) {
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : report_error(CLEFQ_ERR_CUDA, cudaGetErrorString(e));
   }
+  if (a.n_code_dst) return report_error(CLEFQ_ERR_SHAPE, "prepare: extra code destinations need the GEMM-input kernel");
   int tw, ch;
   if (norm) {
     tw = 8;  // the reference's 256-thread reduction order

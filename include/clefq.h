@@ -280,6 +280,57 @@ CLEFQ_API int clefq_tp_gather_unpack(void *stream, const void *codes, int world,
 CLEFQ_API int clefq_tp_interleave(void *stream, const void *src, int world, int64_t rows, int64_t shard_bytes,
                                   void *dst, int64_t dst_ld_bytes);
 
+/*
+ * Symmetric device regions for the ranks of one node (no counterpart in the reference, which
+ * runs on one GPU).  Each rank creates a region of the same size; peers map it through CUDA
+ * IPC handles exchanged by the host (clefq_comm_open), or, when one process drives several
+ * GPUs with peer access enabled, through clefq_comm_attach.  Kernels then store into peers'
+ * regions over NVLink; clefq_comm_barrier orders such phases on the device.  A barrier wait
+ * gives up after the timeout (default 5 s) and clefq_status then reports CLEFQ_ERR_TIMEOUT;
+ * the communicator is out of step after that and must be recreated.
+ */
+typedef struct clefq_comm clefq_comm;
+/* bytes of one IPC handle (the host gathers world of them, in rank order) */
+CLEFQ_API int64_t clefq_comm_handle_bytes(void);
+/* allocates this rank's region of `bytes` (on the current device); handle may be NULL */
+CLEFQ_API int clefq_comm_create(int rank, int world, int64_t bytes, clefq_comm **comm, void *handle);
+/* maps every peer's region from handles[world] (this rank's entry is ignored) */
+CLEFQ_API int clefq_comm_open(clefq_comm *comm, const void *handles);
+/* uses `peer` (rank `rank` of the same group, created in this process) as that rank's region */
+CLEFQ_API int clefq_comm_attach(clefq_comm *comm, int rank, clefq_comm *peer);
+/* 1 when every rank's region is mapped */
+CLEFQ_API int clefq_comm_ready(const clefq_comm *comm);
+CLEFQ_API void *clefq_comm_region(clefq_comm *comm);
+CLEFQ_API int64_t clefq_comm_region_bytes(const clefq_comm *comm);
+CLEFQ_API int clefq_comm_set_timeout_ms(clefq_comm *comm, int64_t ms);
+/* device barrier over the group, ordered on `stream` */
+CLEFQ_API int clefq_comm_barrier(clefq_comm *comm, void *stream);
+CLEFQ_API int clefq_comm_destroy(clefq_comm *comm);
+
+/*
+ * Tensor-parallel MLP block with its collectives inside the kernels (the reference's MLP block,
+ * src/backbone.rs:880-894 and src/quantized.rs:406-439, sharded over the communicator's
+ * ranks).  Rank r passes its shards: gate/up tiled rows [r*I/G, (r+1)*I/G) with their scales,
+ * down tiled rows [r*H/G, (r+1)*H/G); every rank passes the same x [m][hidden] and residual
+ * (nullable) and receives the whole output [m][hidden], bit-identical to clefq_mlp.
+ *   1. pack x; gate|up GEMM of the shard
+ *   2. SwiGLU shard row maxima -> the barrier stores them into every peer and reduces (max)
+ *   3. the shard packed with the full-row maxima; the packing kernel stores its int4 code
+ *      words into every rank's region; barrier; the full code rows unpacked to the s8 operand
+ *   4. down GEMM of the rank's output columns over the full operand; the epilogue stores them
+ *      into every rank's region; barrier; copy to out (skipped when out is
+ *      clefq_tp_mlp_output(), which stays valid until this rank's next call)
+ * Needs I % (256*G) == 0 and H % (256*G) == 0, a region of clefq_tp_mlp_region_bytes and a
+ * workspace of clefq_tp_mlp_workspace_size (both -1 for an unsupported shape).
+ */
+CLEFQ_API int64_t clefq_tp_mlp_region_bytes(int64_t m, int64_t hidden, int64_t inter, int world);
+CLEFQ_API int64_t clefq_tp_mlp_workspace_size(int64_t m, int64_t hidden, int64_t inter, int world);
+CLEFQ_API int clefq_tp_mlp(clefq_comm *comm, void *stream, const void *x, int64_t m, int64_t hidden, int64_t inter,
+                           const void *gate_tiled, const float *gate_scales, const void *up_tiled,
+                           const float *up_scales, const void *down_tiled, const float *down_scales,
+                           const void *residual, void *out, void *workspace, int64_t workspace_bytes);
+CLEFQ_API void *clefq_tp_mlp_output(clefq_comm *comm, int64_t m, int64_t hidden, int64_t inter);
+
 #ifdef __cplusplus
 }
 #endif

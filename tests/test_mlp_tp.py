@@ -6,6 +6,7 @@
   one process (all-reduce and all-gathers done by hand) through every entry point, against
   clefq.mlp; 2 processes over NCCL (needs two GPUs).
 """
+import ctypes
 import os
 import socket
 import sys
@@ -165,3 +166,102 @@ def test_tp_two_ranks_nccl():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     mp.start_processes(_nccl_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
+
+
+# ---------------------------------------------------------------------------------------
+# fused path: clefq_tp_mlp over a TpComm (stores into peers' regions, device barriers)
+# ---------------------------------------------------------------------------------------
+def test_tp_region_and_workspace_sizes():
+    """Host-side shape arithmetic of the fused path (no device work)."""
+    sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
+    import clefq
+    L = clefq.lib()
+    m, h, i = 4096, 4096, 12288
+    for world in (1, 2, 4, 8):
+        region = L.clefq_tp_mlp_region_bytes(m, h, i, world)
+        assert region >= world * m * 4 + m * i // 2 + m * h * 2   # maxima, int4 codes, output
+        assert L.clefq_tp_mlp_workspace_size(m, h, i, world) >= m * (2 * i // world) * 2
+    assert L.clefq_tp_mlp_region_bytes(m, h, 12288 + 256, 2) == -1   # a 256-group would straddle ranks
+    assert L.clefq_tp_mlp_region_bytes(m, 4096 + 256, i, 2) == -1     # odd 128-row tile count per rank
+    assert L.clefq_tp_mlp_region_bytes(m, h, i, 9) == -1              # more ranks than one node
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,residual", [(1, False), (129, True), (4096, True)])
+def test_tp_fused_one_rank_matches_mlp(cq, m, residual):
+    from clefq.tp import TpComm, mlp_tp_fused, shard_mlp, tp_mlp_region_bytes
+    hidden, inter = 1024, 3072
+    gate, up, down = _weights(cq, hidden, inter, 33)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(m + 1)
+    with TpComm(tp_mlp_region_bytes(m, hidden, inter, 1)) as comm:
+        shard = shard_mlp(gate, up, down, 0, 1)
+        for rep in range(3):   # the barrier epochs advance across calls
+            x = torch.randn(m, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+            res = torch.randn(m, hidden, device="cuda", generator=gen).to(torch.bfloat16) if residual else None
+            out = mlp_tp_fused(x, shard, comm, residual=res)
+            ref = cq.mlp(x, gate, up, down, residual=res)
+            assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), f"call {rep}"
+        cq.status()
+
+
+@pytest.mark.gpu
+def test_comm_barrier_times_out_without_peer(cq):
+    """A two-rank group where rank 1 never arrives: rank 0's barrier gives up after the
+    timeout, the status reports it, and the device keeps working."""
+    L = cq.lib()
+    c0, c1 = ctypes.c_void_p(), ctypes.c_void_p()
+    cq._call("clefq_comm_create", 0, 2, 4096, ctypes.byref(c0), None)
+    cq._call("clefq_comm_create", 1, 2, 4096, ctypes.byref(c1), None)
+    try:
+        assert L.clefq_comm_ready(c0) == 0
+        cq._call("clefq_comm_attach", c0, 1, c1)
+        assert L.clefq_comm_ready(c0) == 1
+        cq._call("clefq_comm_set_timeout_ms", c0, 200)
+        cq._call("clefq_comm_barrier", c0, cq._stream())
+        with pytest.raises(RuntimeError, match="gave up"):
+            cq.status()
+        cq.status()   # the status word was cleared by the read
+        x = torch.ones(4, 4, device="cuda")
+        assert float((x @ x).sum()) == 64.0
+    finally:
+        torch.cuda.synchronize()
+        cq._call("clefq_comm_destroy", c0)
+        cq._call("clefq_comm_destroy", c1)
+
+
+def _nccl_fused_worker(rank, world, port):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
+    import clefq as cq
+    from clefq.tp import TpComm, mlp_tp_fused, shard_mlp, tp_mlp_region_bytes
+    torch.cuda.set_device(rank)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        hidden, inter = 2048, 8192
+        gate, up, down = _weights(cq, hidden, inter, 9)
+        shard = shard_mlp(gate, up, down, rank, world)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(5)                       # the same inputs on every rank
+        with TpComm(tp_mlp_region_bytes(1000, hidden, inter, world)) as comm:
+            for m in (1000, 7, 512):
+                x = torch.randn(m, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+                res = torch.randn(m, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+                out = mlp_tp_fused(x, shard, comm, residual=res if m != 7 else None)
+                ref = cq.mlp(x, gate, up, down, residual=res if m != 7 else None)
+                assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), f"rank {rank} m {m}"
+            cq.status()
+            dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_fused_ranks_nccl(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_nccl_fused_worker, args=(world, _free_port()), nprocs=world, join=True,
+                       start_method="spawn")
