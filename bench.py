@@ -297,18 +297,25 @@ def run_clefq(args, world, rank, local):
     traffic = load_traffic().get("gemm_c2_down", {}).get("traffic_bytes")
 
     # ---- end to end through the public API with host buffers ---------------------------
+    # clefq.mlp_host (clefq_mlp_host): pinned host rows in, pinned host rows out; row chunks
+    # stream through the GPU with their PCIe copies overlapping the neighbouring chunks'
+    # kernels.  The chunk size is picked from a few candidates on this box.
     x_host = x.cpu().pin_memory()
     out_host = torch.empty((M, HIDDEN), dtype=torch.bfloat16).pin_memory()
-    x_dev = torch.empty_like(x)
-
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        y = clefq.mlp(x_dev, gate, up, down, workspace=ws)
-        out_host.copy_(y, non_blocking=True)
-    e2e_step()
-    torch.cuda.synchronize()
-    e2e_times = time_steps(e2e_step, max(5, min(args.steps, 50)), flush)
-    e2e_ms = all_max(world, sum(e2e_times) / len(e2e_times))
+    best = None
+    for chunk in (768, 1024, 1152, 1536, 2048):
+        hws = torch.empty(clefq.lib().clefq_mlp_host_workspace_size(chunk, HIDDEN, INTER, 0), dtype=torch.uint8,
+                          device="cuda")
+        e2e_step = lambda: clefq.mlp_host(x_host, gate, up, down, out=out_host, chunk_rows=chunk,  # noqa: E731
+                                          workspace=hws, sync=False)
+        e2e_step()
+        torch.cuda.synchronize()
+        e2e_times = time_steps(e2e_step, max(5, min(args.steps, 50)), flush)
+        t_ms = all_max(world, sum(e2e_times) / len(e2e_times))
+        if best is None or t_ms < best[0]:
+            best = (t_ms, chunk)
+        del hws
+    e2e_ms, e2e_chunk = best
 
     # ---- secondary workload: the C4 MoE layer (8192 tokens, 128 experts, top-8) --------
     moe = None
@@ -395,7 +402,8 @@ def run_clefq(args, world, rank, local):
                      "peak_note": f"kind::i8 dense = 2 x {peak_kind} bf16 burst ({bf16_peak} TF/s) from "
                                   "MEASURED_PEAKS.json"},
         "kernels_ms": ktimes,
-        "e2e": {"value": world * M / (e2e_ms / 1000), "unit": "tokens/s",
+        "e2e": {"value": world * M / (e2e_ms / 1000), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "api": "clefq.mlp_host (clefq_mlp_host), pinned host buffers", "chunk_rows": e2e_chunk,
                 "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(M * HIDDEN * 2)},
         "gpu_launches": launches,
         "clocks": clocks,

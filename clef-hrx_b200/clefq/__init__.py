@@ -45,11 +45,14 @@ _SYMBOLS = {
     "clefq_combine": (ctypes.c_int, ["p", "p", "p", "p", "l", "i", "l", "p"]),
     "clefq_mlp_workspace_size": (ctypes.c_int64, ["l", "l", "l"]),
     "clefq_mlp": (ctypes.c_int, ["p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "p", "l"]),
+    "clefq_mlp_host_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i"]),
+    "clefq_mlp_host": (ctypes.c_int, ["p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "l", "p", "l"]),
     "clefq_moe_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i", "i"]),
     "clefq_moe": (ctypes.c_int, ["p", "p", "p", "i", "l", "l", "l", "i", "i", "p", "p", "p", "p", "p", "p", "p", "p",
                                  "p", "l"]),
     "clefq_moe_ep_record_bytes": (ctypes.c_int64, ["l"]),
-    "clefq_moe_ep_plan": (ctypes.c_int, ["p", "p", "l", "i", "i", "i", "p", "p"]),
+    "clefq_moe_ep_plan_workspace_size": (ctypes.c_int64, ["i"]),
+    "clefq_moe_ep_plan": (ctypes.c_int, ["p", "p", "l", "i", "i", "i", "p", "p", "p", "l"]),
     "clefq_moe_ep_pack": (ctypes.c_int, ["p", "p", "l", "p", "l", "l", "p", "i", "p", "p"]),
     "clefq_moe_ep_experts_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i"]),
     "clefq_moe_ep_experts": (ctypes.c_int, ["p", "p", "l", "l", "l", "i", "i", "p", "p", "p", "p", "p", "p", "p", "p",
@@ -250,7 +253,10 @@ def project_swiglu(gate, up, w: QuantizedWeight, residual=None):
 
 def mlp(x, gate: QuantizedWeight, up: QuantizedWeight, down: QuantizedWeight, residual=None, workspace=None):
     """Dense INT4 SwiGLU MLP block (src/backbone.rs:880-894 + src/quantized.rs:406-439),
-    one C-ABI call: prepare -> gate|up -> fused SwiGLU packing -> down (+ residual)."""
+    one C-ABI call: prepare -> gate|up -> fused SwiGLU packing -> down (+ residual).
+    A host (CPU) x runs through `mlp_host` and returns a host tensor."""
+    if not x.is_cuda:
+        return mlp_host(x, gate, up, down, residual=residual, workspace=workspace)
     m, hidden = x.shape
     inter = gate.rows
     if not (gate.cols == up.cols == hidden and up.rows == inter and down.cols == inter and down.rows == hidden):
@@ -261,6 +267,37 @@ def mlp(x, gate: QuantizedWeight, up: QuantizedWeight, down: QuantizedWeight, re
         workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
     _call("clefq_mlp", _stream(), _ptr(x), m, hidden, inter, _ptr(gate.codes), _ptr(gate.scales), _ptr(up.codes),
           _ptr(up.scales), _ptr(down.codes), _ptr(down.scales), _ptr(residual), _ptr(out), _ptr(workspace), need)
+    return out
+
+
+def mlp_host(x, gate: QuantizedWeight, up: QuantizedWeight, down: QuantizedWeight, residual=None, out=None,
+             chunk_rows=1024, workspace=None, sync=True):
+    """The MLP block from host rows to host rows (clefq_mlp_host): row chunks stream through
+    the GPU with their PCIe copies overlapping the neighbouring chunks' kernels.  x, residual
+    and out are CPU bf16 [m][hidden] (pinned memory for overlap).  With sync=False the call
+    returns once enqueued on the current stream; out is ready when the stream reaches it."""
+    if x.is_cuda or (residual is not None and residual.is_cuda):
+        raise ValueError("mlp_host takes host tensors")
+    m, hidden = x.shape
+    inter = gate.rows
+    if not (gate.cols == up.cols == hidden and up.rows == inter and down.cols == inter and down.rows == hidden):
+        raise ValueError("MLP weight shapes do not chain")
+    x = x.contiguous()
+    if residual is not None:
+        residual = residual.contiguous()
+    if out is None:
+        out = torch.empty((m, hidden), dtype=torch.bfloat16, pin_memory=x.is_pinned())
+    chunk_rows = max(1, min(int(chunk_rows), m))
+    need = lib().clefq_mlp_host_workspace_size(chunk_rows, hidden, inter, int(residual is not None))
+    if need < 0:
+        raise ValueError("unsupported MLP shape")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=gate.codes.device)
+    _call("clefq_mlp_host", _stream(), _ptr(x), m, hidden, inter, _ptr(gate.codes), _ptr(gate.scales), _ptr(up.codes),
+          _ptr(up.scales), _ptr(down.codes), _ptr(down.scales), _ptr(residual), _ptr(out), chunk_rows,
+          _ptr(workspace), need)
+    if sync:
+        torch.cuda.current_stream().synchronize()
     return out
 
 

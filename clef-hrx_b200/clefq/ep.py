@@ -96,11 +96,14 @@ class CudaEpOps:
         return p.codes, p.scales
 
     def plan(self, routes, topk, experts, world):
-        from . import _call, _stream, _ptr
+        from . import _call, _stream, _ptr, lib
         tokens = routes.shape[0]
         counts = torch.empty(world, dtype=torch.int64, device=routes.device)
         slots = torch.empty(max(tokens * topk, 1), dtype=torch.int32, device=routes.device)
-        _call("clefq_moe_ep_plan", _stream(), _ptr(routes), tokens, topk, experts, world, _ptr(counts), _ptr(slots))
+        need = lib().clefq_moe_ep_plan_workspace_size(world)
+        ws = torch.empty(need, dtype=torch.uint8, device=routes.device)
+        _call("clefq_moe_ep_plan", _stream(), _ptr(routes), tokens, topk, experts, world, _ptr(counts), _ptr(slots),
+              _ptr(ws), need)
         return counts, slots
 
     def record_bytes(self, hidden):

@@ -27,7 +27,7 @@ int launch_tp_gather_unpack(const uint32_t *codes, int world, int64_t rows, int 
 int launch_tp_interleave(const uint8_t *src, int world, int64_t rows, int64_t shard_bytes, uint8_t *dst,
                          int64_t dst_ld, cudaStream_t stream, int num_sms);
 int launch_ep_plan(const float *routes, int64_t tokens, int topk, int experts, int world, long long *counts,
-                   int *slots, cudaStream_t stream, int num_sms);
+                   int *slots, int *scratch, cudaStream_t stream);
 int launch_ep_pack(const uint32_t *xq, int64_t words_ld, const float *scales, const float *routes, const int *slots,
                    int64_t tokens, int topk, int code_words, int64_t rec_words, uint32_t *send, cudaStream_t stream,
                    int num_sms);
@@ -324,7 +324,7 @@ int clefq_route(void *stream, const void *logits, int logits_dtype, int64_t toke
 static Arena group_tables(Arena a, int64_t tokens, int topk, int experts, int **counts, int **offsets, int **tiles,
                           int **perm) {
   const int64_t routes = tokens * topk;
-  *counts = a.take<int>(experts);
+  *counts = a.take<int>(experts + sort_scratch_ints(experts));  // counts, then sort scratch
   *offsets = a.take<int>(experts + 1);
   *tiles = a.take<int>(1 + 2 * ((routes + 127) / 128 + experts));
   *perm = a.take<int>(routes > 0 ? routes : 1);
@@ -697,7 +697,7 @@ static Arena moe_tables(Arena a, int64_t tokens, int64_t hidden, int64_t inter, 
   const int64_t routes = tokens * topk;
   t.routes = a.take<float>(tokens * 2 * topk);
   t.order = a.take<float>(tokens * topk);
-  t.counts = a.take<int>(experts);
+  t.counts = a.take<int>(experts + sort_scratch_ints(experts));  // counts, then sort scratch
   t.offsets = a.take<int>(experts + 1);
   t.tiles = a.take<int>(1 + 2 * ((routes + 127) / 128 + experts));
   t.perm = a.take<int>(routes);
@@ -771,14 +771,20 @@ static int check_ep_shape(int64_t tokens, int64_t hidden, int experts, int topk,
   return 0;
 }
 
+int64_t clefq_moe_ep_plan_workspace_size(int world) {
+  return world < 1 || world > 64 ? -1 : (sort_scratch_ints(world) * 4 + 255) & ~int64_t(255);
+}
+
 int clefq_moe_ep_plan(void *stream, const float *routes, int64_t tokens, int topk, int experts, int world,
-                      int64_t *send_counts, int32_t *send_slots) {
+                      int64_t *send_counts, int32_t *send_slots, void *workspace, int64_t workspace_bytes) {
   int rc = check_ep_shape(tokens, 256, experts, topk, world);
   if (rc) return rc;
   if (tokens > 0 && (!routes || !send_slots)) return set_err(CLEFQ_ERR_SHAPE, "null routes or slots");
   if (!send_counts) return set_err(CLEFQ_ERR_SHAPE, "null send counts");
+  if (!workspace || workspace_bytes < clefq_moe_ep_plan_workspace_size(world))
+    return set_err(CLEFQ_ERR_WORKSPACE, "expert-parallel plan workspace too small");
   rc = launch_ep_plan(routes, tokens, topk, experts, world, reinterpret_cast<long long *>(send_counts), send_slots,
-                      static_cast<cudaStream_t>(stream), device_sms());
+                      static_cast<int *>(workspace), static_cast<cudaStream_t>(stream));
   return rc ? cuda_err("expert-parallel plan launch") : 0;
 }
 
@@ -805,7 +811,7 @@ static Arena ep_tables(Arena a, int64_t n, int64_t hidden, int64_t inter, int lo
   const int64_t rows = n > 0 ? n : 1;
   t.routes = a.take<float>(2 * rows);
   t.scales = a.take<float>(rows);
-  t.counts = a.take<int>(local_experts);
+  t.counts = a.take<int>(local_experts + sort_scratch_ints(local_experts));  // counts, then sort scratch
   t.offsets = a.take<int>(local_experts + 1);
   t.tiles = a.take<int>(1 + 2 * ((rows + 127) / 128 + local_experts));
   t.perm = a.take<int>(rows);

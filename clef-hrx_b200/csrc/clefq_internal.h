@@ -122,6 +122,34 @@ struct CommBarrierArgs {
 };
 int launch_comm_barrier(const CommBarrierArgs &a, cudaStream_t stream);
 
+// Stable grouping of route items by key (moe.cu): item i = t * topk + r, key = (int)
+// routes[t * route_ld + r] / key_div; ascending item order within each key.
+constexpr int kSortChunksMax = 296;  // item chunks per sort (two per SM)
+struct SortArgs {
+  const float *routes;
+  int64_t route_ld;          // floats per token row of routes
+  int64_t tokens;            // token rows (the groups layout's row count)
+  int topk;
+  int64_t items;             // item bound (tokens * topk)
+  const int64_t *items_dev;  // optional: actual item count on the device (<= items)
+  int key_div, keys;
+  bool dedupe;               // a token's repeated expert id is grouped once, at its last rank
+  int chunk;                 // set by launch_sort
+  int *hist;                 // scratch [sort_scratch_ints(keys)]
+  int *counts;               // optional outputs
+  long long *counts64;
+  int *offsets;              // [keys + 1]
+  int *tile_list;            // [1 + 2 * tiles]: count, then (key, first position) per tile
+  int tile_rows;
+  int *perm;                 // position -> item
+  int *slots;                // item -> position
+  float *groups;             // reference layout [keys][tokens + 1]
+  float *order;              // [tokens][topk]
+  float *tasks;              // reference 16-row task list
+};
+int64_t sort_scratch_ints(int keys);
+int launch_sort(SortArgs a, cudaStream_t stream);
+
 int device_sms();
 int report_error(int code, const char *msg);  // sets clefq_last_error()
 int *device_status_word();  // per-device zero-initialised status word used by bounded waits

@@ -18,67 +18,25 @@
 
 namespace cq {
 
-// Routes per destination rank (expert / experts_per_rank).
-__global__ void ep_count_kernel(const float *__restrict__ routes, int64_t tokens, int topk, int per_rank, int world,
-                                long long *__restrict__ counts) {
-  const int64_t total = tokens * topk;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / topk;
-    const int r = (int)(i % topk);
-    const int e = (int)routes[t * 2 * topk + r];
-    const int d = e / per_rank;
-    if (e >= 0 && d < world) atomicAdd(reinterpret_cast<unsigned long long *>(&counts[d]), 1ull);
-  }
-}
-
-// One CTA (256 threads) per destination: the send slot of each of its routes, stable in
-// route order (token-major, then rank k), after all routes of lower destinations.
-__global__ void __launch_bounds__(256) ep_slot_kernel(const float *__restrict__ routes, int64_t tokens, int topk,
-                                                      int per_rank, const long long *__restrict__ counts,
-                                                      int *__restrict__ slots) {
-  __shared__ int warp_tot[8];
-  const int d = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  long long base = 0;
-  for (int q = 0; q < d; ++q) base += counts[q];
-  const int64_t total = tokens * topk;
-  long long count0 = 0;
-  for (int64_t i0 = 0; i0 < total; i0 += 256) {
-    const int64_t i = i0 + threadIdx.x;
-    bool match = false;
-    if (i < total) {
-      const int e = (int)routes[(i / topk) * 2 * topk + (i % topk)];
-      match = e >= 0 && e / per_rank == d;
-    }
-    const unsigned ballot = __ballot_sync(0xffffffffu, match);
-    const int in_warp = __popc(ballot & ((1u << lane) - 1u));
-    if (lane == 0) warp_tot[warp] = __popc(ballot);
-    __syncthreads();
-    int before = 0, tot = 0;
-    for (int w = 0; w < 8; ++w) {
-      const int n = warp_tot[w];
-      if (w < warp) before += n;
-      tot += n;
-    }
-    if (match) slots[i] = (int)(base + count0 + before + in_warp);
-    count0 += tot;
-    __syncthreads();
-  }
-}
-
+// Send slots: routes grouped by destination rank (expert / experts_per_rank), stable in
+// route order (token-major, then rank k) -- the stable grouping of moe.cu with the rank as
+// the key.  counts[d] = routes for rank d.
 int launch_ep_plan(const float *routes, int64_t tokens, int topk, int experts, int world, long long *counts,
-                   int *slots, cudaStream_t stream, int num_sms) {
+                   int *slots, int *scratch, cudaStream_t stream) {
   if (world < 1 || world > 64 || experts % world) return CLEFQ_ERR_SHAPE;
-  const int per_rank = experts / world;
-  cudaMemsetAsync(counts, 0, sizeof(long long) * world, stream);
-  const int64_t total = tokens * topk;
-  if (total > 0) {
-    int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 8;
-    ep_count_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(routes, tokens, topk, per_rank, world,
-                                                                                 counts);
-    ep_slot_kernel<<<world, 256, 0, stream>>>(routes, tokens, topk, per_rank, counts, slots);
-  }
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  SortArgs a{};
+  a.routes = routes;
+  a.route_ld = 2 * topk;
+  a.tokens = tokens;
+  a.topk = topk;
+  a.items = tokens * topk;
+  a.key_div = experts / world;
+  a.keys = world;
+  a.dedupe = false;  // one record per route
+  a.hist = scratch;
+  a.counts64 = counts;
+  a.slots = slots;
+  return launch_sort(a, stream);
 }
 
 // One warp per route: the token's packed code row (hidden/8 words), then scale, expert id

@@ -81,127 +81,263 @@ int launch_route(const void *logits, int is_f32, int64_t tokens, int experts, in
   return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
 }
 
-// Counts of routes per expert (ids read from the f32 route table).
-__global__ void count_kernel(const float *__restrict__ routes, int64_t tokens, int topk, int experts,
-                             int *__restrict__ counts) {
-  const int64_t total = tokens * topk;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / topk;
-    const int r = (int)(i % topk);
-    const float *rt = routes + t * 2 * topk;
-    const int e = (int)rt[r];
-    // A token that repeats an expert id is grouped once, at its last matching rank, as
-    // the fill pass does.
-    bool last = true;
-    for (int q = r + 1; q < topk; ++q) last = last && (int)rt[q] != e;
-    if (last && e >= 0 && e < experts) atomicAdd(&counts[e], 1);
-  }
+// ---- stable grouping: a three-phase counting sort of route items by key ----------------
+// Item i = t * topk + r is route r of token t; its key is expert / key_div (an expert id,
+// or the rank owning it).  With dedupe, a token that repeats an expert id is grouped once,
+// at its last matching rank.  The items of each key keep ascending item order, which is the
+// reference's ascending route order within each expert group.
+//   hist:    one CTA per chunk of items: per-key counts of the chunk
+//   scan:    one CTA: per-key totals, offsets, tile list; each chunk's base per key
+//   scatter: one CTA per chunk: stable positions (per-warp sub-ranges in order, lanes of one
+//            key ranked with match.any), written as perm / slots / groups / order
+CQ_DEV int64_t sort_items(const SortArgs &a) {
+  if (!a.items_dev) return a.items;
+  const int64_t n = *a.items_dev;
+  return n < a.items ? (n > 0 ? n : 0) : a.items;
 }
 
-// Single CTA: offsets (exclusive prefix), GEMM tile list (128-row tiles), and optionally
-// the reference-format counts groups[e][0] and 16-row task list.
-__global__ void scan_kernel(const int *__restrict__ counts, int experts, int64_t tokens, int tile_rows,
-                            int *__restrict__ offsets, int *__restrict__ tile_list, float *__restrict__ groups,
-                            float *__restrict__ tasks) {
-  __shared__ int s_off[1025], s_tiles[1025], s_tasks[1025];
-  const int e = threadIdx.x;
-  const int c = e < experts ? counts[e] : 0;
-  if (threadIdx.x == 0) {
-    int run = 0, trun = 0, krun = 0;
-    for (int i = 0; i < experts; ++i) {
-      const int ci = counts[i];
-      s_off[i] = run;
-      s_tiles[i] = trun;
-      s_tasks[i] = krun;
-      run += ci;
-      trun += (ci + tile_rows - 1) / tile_rows;
-      krun += (ci + 15) / 16;
-    }
-    s_off[experts] = run;
-    s_tiles[experts] = trun;
-    s_tasks[experts] = krun;
+CQ_DEV int item_key(const SortArgs &a, int64_t i) {
+  const int64_t t = i / a.topk;
+  const int r = (int)(i % a.topk);
+  const float *rt = a.routes + t * a.route_ld;
+  const int e = (int)rt[r];
+  if (a.dedupe)
+    for (int q = r + 1; q < a.topk; ++q)
+      if ((int)rt[q] == e) return -1;
+  if (e < 0) return -1;
+  const int k = e / a.key_div;
+  return k < a.keys ? k : -1;
+}
+
+__global__ void __launch_bounds__(256) sort_hist_kernel(SortArgs a) {
+  extern __shared__ int sh_count[];
+  for (int k = threadIdx.x; k < a.keys; k += blockDim.x) sh_count[k] = 0;
+  __syncthreads();
+  const int64_t n = sort_items(a);
+  const int64_t lo = (int64_t)blockIdx.x * a.chunk;
+  const int64_t hi = lo + a.chunk < n ? lo + a.chunk : n;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const int k = item_key(a, i);
+    if (k >= 0) atomicAdd(&sh_count[k], 1);
   }
   __syncthreads();
-  if (e < experts) {
-    offsets[e] = s_off[e];
-    for (int i = 0; i < (c + tile_rows - 1) / tile_rows; ++i) {
-      tile_list[1 + 2 * (s_tiles[e] + i)] = e;
-      tile_list[2 + 2 * (s_tiles[e] + i)] = s_off[e] + tile_rows * i;
+  for (int k = threadIdx.x; k < a.keys; k += blockDim.x) a.hist[(int64_t)k * gridDim.x + blockIdx.x] = sh_count[k];
+}
+
+// Exclusive block-wide prefix sum of one value per thread (1024 threads at most); returns
+// (prefix, block total).
+CQ_DEV int2 block_exclusive_scan(int v, int *warp_sums) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
+  int x = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nwarps ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += y;
     }
-    if (groups) groups[(int64_t)e * (tokens + 1)] = (float)c;
-    if (tasks) {
-      for (int i = 0; i < (c + 15) / 16; ++i) {
-        tasks[1 + 2 * (s_tasks[e] + i)] = (float)e;
-        tasks[2 + 2 * (s_tasks[e] + i)] = (float)(16 * i);
+    warp_sums[lane] = w;  // inclusive prefix over warps
+  }
+  __syncthreads();
+  const int total = warp_sums[nwarps - 1];
+  const int before = warp == 0 ? 0 : warp_sums[warp - 1];
+  __syncthreads();
+  return make_int2(before + x - v, total);
+}
+
+// hist is key-major ([keys][chunks]).  Warps sum each key's chunk counts, each thread scans
+// two adjacent keys (2t and 2t+1), and warps turn each key's chunk counts into the chunks'
+// first positions; every warp issues its loads of a key at once (chunks <= 320).
+constexpr int kSortChunkRegs = (kSortChunksMax + 31) / 32;
+__global__ void __launch_bounds__(512, 1) sort_scan_kernel(const __grid_constant__ SortArgs a, int chunks) {
+  __shared__ int warp_sums[32];
+  __shared__ int s_key[1024];  // per-key totals, then offsets
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int e = warp; e < a.keys; e += nwarps) {
+    const int *h = a.hist + (int64_t)e * chunks;
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < kSortChunkRegs; ++j) {
+      const int q = lane + 32 * j;
+      if (q < chunks) c += h[q];
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+    if (lane == 0) s_key[e] = c;
+  }
+  __syncthreads();
+  const int e0 = 2 * threadIdx.x;
+  int c[2], off[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) c[j] = e0 + j < a.keys ? s_key[e0 + j] : 0;
+  const int2 r0 = block_exclusive_scan(c[0] + c[1], warp_sums);
+  off[0] = r0.x;
+  off[1] = off[0] + c[0];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int e = e0 + j;
+    if (e >= a.keys) continue;
+    if (a.counts) a.counts[e] = c[j];
+    if (a.counts64) a.counts64[e] = c[j];
+    if (a.offsets) a.offsets[e] = off[j];
+    if (a.groups) a.groups[(int64_t)e * (a.tokens + 1)] = (float)c[j];
+    s_key[e] = off[j];
+  }
+  if (threadIdx.x == 0 && a.offsets) a.offsets[a.keys] = r0.y;
+  if (a.tile_list) {
+    const int t0 = (c[0] + a.tile_rows - 1) / a.tile_rows, t1 = (c[1] + a.tile_rows - 1) / a.tile_rows;
+    const int2 r = block_exclusive_scan(t0 + t1, warp_sums);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int n = j ? t1 : t0, base = j ? r.x + t0 : r.x;
+      for (int i = 0; i < n; ++i) {
+        a.tile_list[1 + 2 * (base + i)] = e0 + j;
+        a.tile_list[2 + 2 * (base + i)] = off[j] + a.tile_rows * i;
       }
     }
+    if (threadIdx.x == 0) a.tile_list[0] = r.y;
   }
-  if (threadIdx.x == 0) {
-    offsets[experts] = s_off[experts];
-    tile_list[0] = s_tiles[experts];
-    if (tasks) tasks[0] = (float)s_tasks[experts];
+  if (a.tasks) {
+    const int k0 = (c[0] + 15) / 16, k1 = (c[1] + 15) / 16;
+    const int2 r = block_exclusive_scan(k0 + k1, warp_sums);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int n = j ? k1 : k0, base = j ? r.x + k0 : r.x;
+      for (int i = 0; i < n; ++i) {
+        a.tasks[1 + 2 * (base + i)] = (float)(e0 + j);
+        a.tasks[2 + 2 * (base + i)] = (float)(16 * i);
+      }
+    }
+    if (threadIdx.x == 0) a.tasks[0] = (float)r.y;
+  }
+  __syncthreads();
+  // hist[e][q] := first position of key e's items in chunk q
+  for (int e = warp; e < a.keys; e += nwarps) {
+    int *h = a.hist + (int64_t)e * chunks;
+    int v[kSortChunkRegs];
+#pragma unroll
+    for (int j = 0; j < kSortChunkRegs; ++j) {
+      const int q = lane + 32 * j;
+      v[j] = q < chunks ? h[q] : 0;
+    }
+    int carry = s_key[e];
+#pragma unroll
+    for (int j = 0; j < kSortChunkRegs; ++j) {
+      int x = v[j];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      const int q = lane + 32 * j;
+      if (q < chunks) h[q] = carry + x - v[j];
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
   }
 }
 
-// One CTA (256 threads) per expert: stable compaction in token order.
-__global__ void __launch_bounds__(256) fill_kernel(const float *__restrict__ routes, int64_t tokens, int topk,
-                                                   const int *__restrict__ offsets, float *__restrict__ groups,
-                                                   float *__restrict__ order, int *__restrict__ perm) {
-  __shared__ int warp_tot[8];
-  const int e = blockIdx.x;
+__global__ void __launch_bounds__(256) sort_scatter_kernel(SortArgs a) {
+  extern __shared__ int sh_base[];  // [8 warps][keys]: next position per key for each warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int base = offsets[e];
-  const float ef = (float)e;
-  int count0 = 0;
-  for (int64_t t0 = 0; t0 < tokens; t0 += 256) {
-    const int64_t t = t0 + threadIdx.x;
-    int rank = topk, less = 0;
-    if (t < tokens) {
-      const float *rt = routes + t * 2 * topk;
-      for (int r = 0; r < topk; ++r) {
-        const float id = rt[r];
-        if ((int)id == e) rank = r;
-        if (id < ef) ++less;
-      }
-    }
-    const bool match = rank < topk;
-    const unsigned ballot = __ballot_sync(0xffffffffu, match);
-    const int in_warp = __popc(ballot & ((1u << lane) - 1u));
-    if (lane == 0) warp_tot[warp] = __popc(ballot);
-    __syncthreads();
-    int before = 0, total = 0;
-    for (int w = 0; w < 8; ++w) {
-      const int n = warp_tot[w];
-      if (w < warp) before += n;
-      total += n;
-    }
-    if (match) {
-      const int ordinal = count0 + before + in_warp;
-      const int route = (int)(t * topk + rank);
-      if (groups) groups[(int64_t)e * (tokens + 1) + 1 + ordinal] = (float)route;
-      if (perm) perm[base + ordinal] = route;
-      if (order) order[t * topk + less] = (float)rank;
-    }
-    count0 += total;
-    __syncthreads();
+  for (int j = threadIdx.x; j < 8 * a.keys; j += blockDim.x) sh_base[j] = 0;
+  __syncthreads();
+  const int64_t n = sort_items(a);
+  const int64_t lo = (int64_t)blockIdx.x * a.chunk;
+  const int64_t hi = lo + a.chunk < n ? lo + a.chunk : n;
+  const int per_warp = a.chunk / 8;
+  const int64_t wlo = lo + (int64_t)warp * per_warp;
+  const int64_t whi = wlo + per_warp < hi ? wlo + per_warp : hi;
+  int *mine = sh_base + warp * a.keys;
+  for (int64_t i = wlo + lane; i < whi; i += 32) {
+    const int k = item_key(a, i);
+    if (k >= 0) atomicAdd(&mine[k], 1);
   }
+  __syncthreads();
+  for (int k = threadIdx.x; k < a.keys; k += blockDim.x) {
+    int run = a.hist[(int64_t)k * gridDim.x + blockIdx.x];
+    for (int w = 0; w < 8; ++w) {
+      const int c = sh_base[w * a.keys + k];
+      sh_base[w * a.keys + k] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  const unsigned lt = (1u << lane) - 1u;
+  for (int64_t i0 = wlo; i0 < whi; i0 += 32) {
+    const int64_t i = i0 + lane;
+    const int k = i < whi ? item_key(a, i) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, k);
+    const int rank = __popc(peers & lt);
+    const int pos = k >= 0 ? mine[k] + rank : -1;
+    __syncwarp();
+    if (k >= 0 && rank == 0) mine[k] += __popc(peers);
+    __syncwarp();
+    if (k < 0) continue;
+    if (a.perm) a.perm[pos] = (int)i;
+    if (a.slots) a.slots[i] = pos;
+    if (a.groups) a.groups[(int64_t)k * (a.tokens + 1) + 1 + (pos - a.offsets[k])] = (float)i;
+    if (a.order) {
+      // order[t][j] = the rank holding the token's j-th smallest expert id
+      const int64_t t = i / a.topk;
+      const float *rt = a.routes + t * a.route_ld;
+      const float id = rt[i % a.topk];
+      int less = 0;
+      for (int q = 0; q < a.topk; ++q) less += rt[q] < id;
+      a.order[t * a.topk + less] = (float)(i % a.topk);
+    }
+  }
+}
+
+int64_t sort_scratch_ints(int keys) { return (int64_t)kSortChunksMax * keys; }
+
+int launch_sort(SortArgs a, cudaStream_t stream) {
+  if (a.keys < 1 || a.keys > 1024 || a.topk < 1 || a.key_div < 1 || !a.hist) return CLEFQ_ERR_SHAPE;
+  // chunks of whole 256-item rounds, at most kSortChunksMax of them
+  int64_t chunk = (a.items + kSortChunksMax - 1) / kSortChunksMax;
+  chunk = ((chunk + 255) / 256) * 256;
+  if (chunk < 256) chunk = 256;
+  if (chunk > 0x7fffffff) return CLEFQ_ERR_SHAPE;
+  a.chunk = (int)chunk;
+  const int chunks = a.items > 0 ? (int)((a.items + chunk - 1) / chunk) : 0;
+  if (chunks > 0)
+    sort_hist_kernel<<<chunks, 256, sizeof(int) * a.keys, stream>>>(a);
+  sort_scan_kernel<<<1, 512, 0, stream>>>(a, chunks);
+  if (chunks > 0)
+    sort_scatter_kernel<<<chunks, 256, sizeof(int) * 8 * a.keys, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
 }
 
 int launch_group(const float *routes, int64_t tokens, int topk, int experts, int tile_rows, int *counts, int *offsets,
                  int *tile_list, int *perm, float *groups, float *order, float *tasks, cudaStream_t stream,
                  int num_sms) {
+  (void)num_sms;
   if (experts > 1024 || topk <= 0) return CLEFQ_ERR_SHAPE;
-  cudaMemsetAsync(counts, 0, sizeof(int) * experts, stream);
-  if (tokens > 0) {
-    const int64_t total = tokens * topk;
-    int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 8;
-    count_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(routes, tokens, topk, experts, counts);
-  }
-  scan_kernel<<<1, experts <= 32 ? 32 : ((experts + 31) / 32) * 32, 0, stream>>>(counts, experts, tokens, tile_rows,
-                                                                                 offsets, tile_list, groups, tasks);
-  if (tokens > 0)
-    fill_kernel<<<experts, 256, 0, stream>>>(routes, tokens, topk, offsets, groups, order, perm);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  SortArgs a{};
+  a.routes = routes;
+  a.route_ld = 2 * topk;
+  a.tokens = tokens;
+  a.topk = topk;
+  a.items = tokens * topk;
+  a.key_div = 1;
+  a.keys = experts;
+  a.dedupe = true;
+  a.hist = counts + experts;
+  a.counts = counts;
+  a.offsets = offsets;
+  a.tile_list = tile_list;
+  a.tile_rows = tile_rows;
+  a.perm = perm;
+  a.groups = groups;
+  a.order = order;
+  a.tasks = tasks;
+  return launch_sort(a, stream);
 }
 
 // Reference-format task list from a reference-format groups buffer (counts in groups[e][0]).

@@ -200,6 +200,20 @@ CLEFQ_API int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, 
                         const float *gate_scales, const void *up_tiled, const float *up_scales, const void *down_tiled,
                         const float *down_scales, const void *residual, void *out, void *workspace,
                         int64_t workspace_bytes);
+/*
+ * clefq_mlp from host memory to host memory: x, residual (nullable) and out are host
+ * buffers [m][hidden] (pinned for the copies to overlap).  The rows run in chunks of
+ * chunk_rows; each chunk's host->device copy, kernels and device->host copy overlap those of
+ * its neighbours (library-owned copy streams).  Rows are independent, so the output equals
+ * clefq_mlp's.  Ordered on `stream`: out is complete once the stream reaches that point.
+ * workspace >= clefq_mlp_host_workspace_size(chunk_rows, hidden, inter, residual != NULL).
+ */
+CLEFQ_API int64_t clefq_mlp_host_workspace_size(int64_t chunk_rows, int64_t hidden, int64_t inter, int with_residual);
+CLEFQ_API int clefq_mlp_host(void *stream, const void *x_host, int64_t m, int64_t hidden, int64_t inter,
+                             const void *gate_tiled, const float *gate_scales, const void *up_tiled,
+                             const float *up_scales, const void *down_tiled, const float *down_scales,
+                             const void *residual_host, void *out_host, int64_t chunk_rows, void *workspace,
+                             int64_t workspace_bytes);
 
 /*
  * Omni INT4 MoE block; replaces the expert part of forward_layers_cached
@@ -232,9 +246,11 @@ CLEFQ_API int clefq_moe(void *stream, const void *x, const void *logits, int log
  * The result is bit-identical to clefq_moe on one GPU.
  */
 CLEFQ_API int64_t clefq_moe_ep_record_bytes(int64_t hidden);
-/* routes f32 [tokens][2*topk] from clefq_route; send_counts int64 [world]; send_slots int32 [tokens*topk] */
+/* routes f32 [tokens][2*topk] from clefq_route; send_counts int64 [world]; send_slots int32 [tokens*topk];
+ * workspace of clefq_moe_ep_plan_workspace_size(world) bytes */
+CLEFQ_API int64_t clefq_moe_ep_plan_workspace_size(int world);
 CLEFQ_API int clefq_moe_ep_plan(void *stream, const float *routes, int64_t tokens, int topk, int experts, int world,
-                                int64_t *send_counts, int32_t *send_slots);
+                                int64_t *send_counts, int32_t *send_slots, void *workspace, int64_t workspace_bytes);
 /* a_codes/a_ld_words/a_scales: packed int4 rows of the tokens (clefq_prepare storage) */
 CLEFQ_API int clefq_moe_ep_pack(void *stream, const void *a_codes, int64_t a_ld_words, const float *a_scales,
                                 int64_t tokens, int64_t hidden, const float *routes, int topk,

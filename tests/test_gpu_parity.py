@@ -253,6 +253,39 @@ def test_mlp_block(cq):
     cq.status()
 
 
+@pytest.mark.parametrize("chunk,pinned,residual", [(64, True, False), (77, True, True), (200, False, True),
+                                                   (1000, True, False)])
+def test_mlp_block_host_chunks(cq, chunk, pinned, residual):
+    """Host-to-host MLP (clefq_mlp_host): row chunks streamed through the GPU give the
+    oracle's block bit for bit, for chunk sizes that do and do not divide the rows."""
+    rng = np.random.default_rng(chunk)
+    m, h, inter = 200, 1024, 768
+    ws = []
+    for n, k in ((inter, h), (inter, h), (h, inter)):
+        _, wt, s, dev = _weight(rng, n, k)
+        ws.append(((wt, s, n), dev))
+    x = bf16_normal(rng, (m, h))
+    res = bf16_normal(rng, (m, h)) if residual else None
+    if res is None:
+        ref = o.mlp_block(x, ws[0][0], ws[1][0], ws[2][0])
+    else:  # the oracle's steps with the residual fused into the down projection
+        _, xc, xs, _ = o.prepare(x, 4, o.stride_for(h))
+        g = o.gemm(xc, xs, *ws[0][0], h)
+        u = o.gemm(xc, xs, *ws[1][0], h)
+        _, hc, hs, _ = o.prepare(o.swiglu(g, u), 4, o.stride_for(inter))
+        ref = o.gemm(hc, hs, *ws[2][0], inter, residual=res)
+
+    def host(a):
+        t = torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
+        return t.pin_memory() if pinned else t
+    for _ in range(2):
+        out = cq.mlp_host(host(x), ws[0][1], ws[1][1], ws[2][1], residual=None if res is None else host(res),
+                          chunk_rows=chunk)
+        assert not out.is_cuda
+        assert np.array_equal(out.view(torch.int16).numpy().view(np.uint16), ref)
+    cq.status()
+
+
 # ---------------------------------------------------------------------------------------
 # MoE operators
 # ---------------------------------------------------------------------------------------
