@@ -323,14 +323,31 @@ def run_clefq(args, world, rank, local):
         mx = torch.randn(MOE_T, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
         wr = torch.randn(MOE_E, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
         logits = mx @ wr.t()     # router linear (BF16, cuBLAS): outside the INT4 path
+        nccl_ms = None
         if world > 1:
-            # expert parallel: this rank owns MOE_E / world experts and its own MOE_T tokens
-            from clefq.ep import ExpertShard, omni_moe_ep
+            # expert parallel: this rank owns MOE_E / world experts and its own MOE_T tokens;
+            # one clefq_moe_ep_layer call per step (records and products stored into the peers'
+            # symmetric buffers by the kernels), the NCCL all-to-all composition timed beside it
+            from clefq.comm import Comm
+            from clefq.ep import ExpertShard, ep_layer_region_bytes, omni_moe_ep, omni_moe_ep_fused
             per = MOE_E // world
             shard = ExpertShard(rand_weight_dev(clefq, per * MOE_I, MOE_H, gen),
                                 rand_weight_dev(clefq, per * MOE_I, MOE_H, gen),
                                 rand_weight_dev(clefq, per * MOE_H, MOE_I, gen), rank * per, per, MOE_E, MOE_I)
-            mstep = lambda: omni_moe_ep(mx, logits, shard, MOE_K)   # noqa: E731
+            cap = world * MOE_T * MOE_K
+            ecomm = Comm(ep_layer_region_bytes(MOE_T, MOE_H, MOE_K, world, cap))
+            ews = torch.empty(clefq.lib().clefq_moe_ep_layer_workspace_size(MOE_T, MOE_H, MOE_I, MOE_E, MOE_K, world,
+                                                                            cap), dtype=torch.uint8, device="cuda")
+            eout = torch.empty((MOE_T, MOE_H), dtype=torch.bfloat16, device="cuda")
+            nstep = lambda: omni_moe_ep(mx, logits, shard, MOE_K)   # noqa: E731
+            for _ in range(3):
+                nstep()
+            torch.cuda.synchronize()
+            barrier(world)
+            nt = time_steps(nstep, max(5, min(args.steps, 30)), flush)
+            nccl_ms = all_max(world, sum(nt) / len(nt))
+            mstep = lambda: omni_moe_ep_fused(mx, logits, shard, ecomm, MOE_K, recv_cap=cap,  # noqa: E731
+                                              workspace=ews, out=eout)
         else:
             mg = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
             mu = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
@@ -342,13 +359,19 @@ def run_clefq(args, world, rank, local):
             mstep()
         torch.cuda.synchronize()
         clefq.status()
+        barrier(world)
         mt = time_steps(mstep, max(5, min(args.steps, 30)), flush)
+        clefq.status()
         mms = all_max(world, sum(mt) / len(mt))
+        if world > 1:
+            ecomm.close()
         ops = 2.0 * MOE_T * MOE_K * (MOE_H * 2 * MOE_I + MOE_I * MOE_H)
         moe = {"workload": "C4 Omni INT4 MoE layer: 8192 tokens per GPU, hidden 2048, 128 experts x (gate|up "
                            "2048->2x768, down 768->2048), top-8",
-               "parallelism": f"ep{world} (experts sharded, NCCL all-to-all dispatch/combine)" if world > 1
+               "parallelism": f"ep{world}: experts sharded; one clefq_moe_ep_layer call, dispatch and return "
+                              "stored into peers' buffers over NVLink by the kernels" if world > 1
                else "single GPU", "tokens_per_s": world * MOE_T / (mms / 1000), "ms_per_step": mms,
+               "nccl_all_to_all_ms_per_step": nccl_ms,
                "tops": ops / (mms / 1000) / 1e12, "frac_of_int8_peak": ops / (mms / 1000) / 1e12 / i8_peak}
 
     # ---- tensor-parallel C2 block (N > 1): one 4096-token block shared by all ranks -------

@@ -76,6 +76,10 @@ _SYMBOLS = {
     "clefq_tp_mlp_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i"]),
     "clefq_tp_mlp": (ctypes.c_int, ["p", "p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "p", "l"]),
     "clefq_tp_mlp_output": (ctypes.c_void_p, ["p", "l", "l", "l"]),
+    "clefq_moe_ep_layer_region_bytes": (ctypes.c_int64, ["l", "l", "i", "i", "l"]),
+    "clefq_moe_ep_layer_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i", "i", "i", "l"]),
+    "clefq_moe_ep_layer": (ctypes.c_int, ["p", "p", "p", "p", "i", "l", "l", "l", "i", "i", "l", "p", "p", "p", "p", "p",
+                                          "p", "p", "p", "p", "l"]),
 }
 _CT = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64}
 

@@ -160,3 +160,44 @@ def omni_moe_ep(x: torch.Tensor, logits: torch.Tensor, shard: ExpertShard, topk:
     back = torch.empty(max(n_send, 1), hidden, dtype=torch.bfloat16, device=products.device)
     _exchange(back, products, sc, rc, group)
     return ops.combine(back, slots, routes, topk, hidden), routes
+
+
+def ep_layer_region_bytes(tokens: int, hidden: int, topk: int, world: int, recv_cap: int) -> int:
+    from . import lib
+    n = lib().clefq_moe_ep_layer_region_bytes(tokens, hidden, topk, world, recv_cap)
+    if n < 0:
+        raise ValueError("unsupported expert-parallel MoE layer shape")
+    return n
+
+
+def omni_moe_ep_fused(x: torch.Tensor, logits: torch.Tensor, shard: ExpertShard, comm, topk: int = 8,
+                      recv_cap: int | None = None, workspace=None, out=None):
+    """Expert-parallel Omni MoE block in one C-ABI call (clefq_moe_ep_layer) over a
+    `clefq.comm.Comm`: records and products are stored straight into the other ranks'
+    symmetric buffers by the dispatch kernel and the expert down-GEMM epilogue, with no host
+    synchronisation.  recv_cap (the same on every rank) defaults to world * tokens * topk, which
+    always suffices when every rank has `tokens` tokens.  Returns (out, routes)."""
+    from . import BF16, F32, _call, _need_cuda, _ptr, _stream, lib
+    _need_cuda(x, logits)
+    tokens, hidden = x.shape
+    world = comm.world
+    if shard.count * world != shard.experts or shard.base != comm.rank * shard.count:
+        raise ValueError("expert shard does not match the communicator")
+    if recv_cap is None:
+        recv_cap = world * tokens * topk
+    x = x.contiguous()
+    logits = logits.contiguous()
+    dt = F32 if logits.dtype == torch.float32 else BF16
+    need = lib().clefq_moe_ep_layer_workspace_size(tokens, hidden, shard.inter, shard.experts, topk, world, recv_cap)
+    if need < 0:
+        raise ValueError("unsupported expert-parallel MoE layer shape")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    if out is None:
+        out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=x.device)
+    routes = torch.empty((tokens, 2 * topk), dtype=torch.float32, device=x.device)
+    _call("clefq_moe_ep_layer", comm.handle, _stream(), _ptr(x), _ptr(logits), dt, tokens, hidden, shard.inter,
+          shard.experts, topk, recv_cap, _ptr(shard.gate.codes), _ptr(shard.gate.scales), _ptr(shard.up.codes),
+          _ptr(shard.up.scales), _ptr(shard.down.codes), _ptr(shard.down.scales), _ptr(out), _ptr(routes),
+          _ptr(workspace), need)
+    return out, routes

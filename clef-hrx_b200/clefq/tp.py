@@ -20,11 +20,12 @@ straight into every rank's symmetric buffer over NVLink, ordered by device barri
 """
 from __future__ import annotations
 
-import ctypes
 from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
+
+from .comm import Comm, all_gather_rows as _all_gather
 
 
 @dataclass
@@ -54,14 +55,6 @@ def shard_mlp(gate, up, down, rank: int, world: int) -> MlpShard:
                                w.stride, w.bits)
     return MlpShard(cut(gate, inter // world), cut(up, inter // world), cut(down, hidden // world), rank, world,
                     hidden, inter)
-
-
-def _all_gather(out: torch.Tensor, inp: torch.Tensor, group):
-    """out[g] = inp of rank g (out has a leading world dimension)."""
-    if dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(out, inp.contiguous(), group=group)
-    else:
-        dist.all_gather(list(out.unbind(0)), inp.contiguous(), group=group)
 
 
 class CudaTpOps:
@@ -155,57 +148,7 @@ def mlp_tp(x: torch.Tensor, shard: MlpShard, residual=None, group=None, ops=None
     return ops.interleave(out_all)
 
 
-class TpComm:
-    """This rank's symmetric region, mapped into every rank of `group` (clefq_comm_*).
-
-    Collective: every rank constructs it with the same `region_bytes` (at least
-    `tp_mlp_region_bytes` of the largest block it will run).  Without an initialised process
-    group it is a one-rank communicator."""
-
-    def __init__(self, region_bytes: int, group=None, timeout_ms: int | None = None):
-        from . import _call, lib
-        distributed = dist.is_available() and dist.is_initialized()
-        self.rank = dist.get_rank(group) if distributed else 0
-        self.world = dist.get_world_size(group) if distributed else 1
-        self.region_bytes = int(region_bytes)
-        hb = lib().clefq_comm_handle_bytes()
-        handle = ctypes.create_string_buffer(hb)
-        self._comm = ctypes.c_void_p()
-        _call("clefq_comm_create", self.rank, self.world, self.region_bytes, ctypes.byref(self._comm), handle)
-        if self.world > 1:
-            dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" else "cpu"
-            mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(dev)
-            every = torch.empty((self.world, hb), dtype=torch.uint8, device=dev)
-            _all_gather(every, mine, group)
-            _call("clefq_comm_open", self._comm, ctypes.create_string_buffer(every.cpu().numpy().tobytes()))
-        if timeout_ms:
-            _call("clefq_comm_set_timeout_ms", self._comm, int(timeout_ms))
-        if self.world > 1:
-            dist.barrier(group)
-
-    @property
-    def handle(self):
-        if self._comm is None:
-            raise RuntimeError("TpComm is closed")
-        return self._comm
-
-    def barrier(self):
-        from . import _call, _stream
-        _call("clefq_comm_barrier", self.handle, _stream())
-
-    def close(self):
-        """Releases the region (after the device is done with it); not collective."""
-        from . import _call
-        if self._comm is not None:
-            torch.cuda.synchronize()
-            _call("clefq_comm_destroy", self._comm)
-            self._comm = None
-
-    def __enter__(self):
-        return self
-
-    def __exit__(self, *exc):
-        self.close()
+TpComm = Comm  # the communicator of the fused path (clefq.comm)
 
 
 def tp_mlp_region_bytes(m: int, hidden: int, inter: int, world: int) -> int:

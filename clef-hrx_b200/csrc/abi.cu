@@ -19,9 +19,10 @@ int launch_groups_to_sorted(const float *groups, int64_t tokens, int topk, int e
 int launch_gather(const uint8_t *src, int64_t src_ld, const int *perm, int div, int64_t rows, int64_t row_bytes,
                   uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms);
 int launch_gather_unpack_i4(const uint32_t *a, int64_t a_ld, const int *perm, int div, int64_t rows, int k,
-                            uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms);
+                            uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms,
+                            const int64_t *rows_dev = nullptr);
 int launch_combine(const uint16_t *values, const float *routes, const float *order, int64_t tokens, int topk,
-                   int64_t width, uint16_t *out, cudaStream_t stream, int num_sms);
+                   int64_t width, uint16_t *out, cudaStream_t stream, int num_sms, bool weighted = false);
 int launch_tp_gather_unpack(const uint32_t *codes, int world, int64_t rows, int shard_words, uint8_t *op,
                             int64_t op_ld, cudaStream_t stream, int num_sms);
 int launch_tp_interleave(const uint8_t *src, int world, int64_t rows, int64_t shard_bytes, uint8_t *dst,
@@ -109,7 +110,7 @@ static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_
                        int64_t aux_ld, int64_t rows, int64_t width, int64_t stride, void *out, void *operand,
                        int64_t operand_ld, void *norm_out, int64_t norm_ld, float *rowmax_out = nullptr,
                        const float *rowmax_in = nullptr, uint32_t *const *code_dst = nullptr,
-                       int n_code_dst = 0, int64_t code_ld = 0) {
+                       int n_code_dst = 0, int64_t code_ld = 0, const int64_t *rows_dev = nullptr) {
   int rc = check_prepare(kind, bits, rows, width, stride);
   if (rc) return rc;
   if (!x || (!out && !rowmax_out) || (kind != CLEFQ_PREP_PLAIN && !aux) ||
@@ -150,6 +151,7 @@ static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_
   for (int d = 0; d < n_code_dst; ++d) a.code_dst[d] = code_dst[d];
   a.n_code_dst = n_code_dst;
   a.code_ld = code_ld;
+  a.rows_dev = rows_dev;
   return launch_prepare(a, s);  // sets clefq_last_error() itself on failure
 }
 
@@ -627,11 +629,21 @@ void *clefq_tp_mlp_output(clefq_comm *c, int64_t m, int64_t hidden, int64_t inte
 // ---- grouped expert FFN shared by the fused MoE block and the expert-parallel path ----
 // xs: expert-sorted s8 operand rows (route order given by perm); a_scales: the token
 // scale of route r at a_scales[r / topk].  Writes values[route] = down(SwiGLU(gate|up)).
+// Expert-parallel variant: nroutes is the capacity, rows_dev the routes present (on the
+// device), and `ret` sends each route's bf16(value * probability) to its home rank.
+struct ExpertReturn {
+  const int64_t *rows_dev;
+  uint16_t *base[kMaxRanks];
+  const int *rank, *row;
+  const float *prob;
+};
+
 static int run_expert_ffn(cudaStream_t s, const uint8_t *xs, int64_t nroutes, const float *a_scales, int topk,
                           const int *tiles, const int *offsets, const int *perm, int experts, int tile_rows,
                           int64_t hidden, int64_t inter, const void *gate_tiled, const float *gate_scales,
                           const void *up_tiled, const float *up_scales, const void *down_tiled,
-                          const float *down_scales, uint16_t *gu, uint32_t *hq, uint8_t *h8, uint16_t *values) {
+                          const float *down_scales, uint16_t *gu, uint32_t *hq, uint8_t *h8, uint16_t *values,
+                          const ExpertReturn *ret = nullptr) {
   int *status = device_status_word();
   if (!status) return cuda_err("status word");
   GemmParams p{};
@@ -664,7 +676,7 @@ static int run_expert_ffn(cudaStream_t s, const uint8_t *xs, int64_t nroutes, co
   if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert gate/up launch") : set_err(rc, "expert gate/up shape");
   // SwiGLU fused into the packing of the hidden rows (still expert-sorted).
   rc = run_prepare(s, CLEFQ_PREP_SWIGLU, 4, gu, 2 * inter, gu + inter, 2 * inter, nroutes, inter, inter, hq, h8, inter,
-                   nullptr, 0);
+                   nullptr, 0, nullptr, nullptr, nullptr, 0, 0, ret ? ret->rows_dev : nullptr);
   if (rc) return rc;
   p.a_op = h8;
   p.a_ld = inter;
@@ -680,6 +692,12 @@ static int run_expert_ffn(cudaStream_t s, const uint8_t *xs, int64_t nroutes, co
   p.ldo = hidden;
   p.scale_mode = 0;  // hidden rows were packed in sorted order
   p.scatter = 1;     // values land at their route id
+  if (ret) {
+    for (int g = 0; g < kMaxRanks; ++g) p.ret_base[g] = ret->base[g];
+    p.ret_rank = ret->rank;
+    p.ret_row = ret->row;
+    p.ret_prob = ret->prob;
+  }
   rc = launch_gemm(p, s);
   if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert down launch") : set_err(rc, "expert down shape");
   return 0;
@@ -871,6 +889,219 @@ int clefq_moe_ep_combine(void *stream, const void *products, const int32_t *send
   rc = launch_ep_combine(static_cast<const uint16_t *>(products), send_slots, routes, tokens, topk, hidden,
                          static_cast<uint16_t *>(out), static_cast<cudaStream_t>(stream), device_sms());
   return rc ? cuda_err("expert-parallel combine launch") : 0;
+}
+
+// ---- expert-parallel Omni MoE layer, exchanges fused into its kernels --------------------
+// Symmetric region (same offsets on every rank): the counts matrix int [world][world], the
+// receive buffer [recv_cap][record], then this rank's products [tokens * topk][hidden] BF16
+// (written by the expert ranks' down-GEMM epilogues at the home route index).
+static Arena ep_region(Arena a, int64_t tokens, int64_t hidden, int topk, int world, int64_t recv_cap, int **counts,
+                       uint32_t **recv, uint16_t **products) {
+  *counts = a.take<int>((int64_t)world * world);
+  *recv = a.take<uint32_t>(recv_cap * (clefq_moe_ep_record_bytes(hidden) / 4));
+  *products = a.take<uint16_t>((tokens > 0 ? tokens : 1) * topk * hidden);
+  return a;
+}
+
+struct EpLayerTables {
+  float *routes, *xs_scales, *rmeta, *ret_prob;
+  uint32_t *xq, *hq;
+  int *slots, *scratch, *offsets, *tiles, *perm, *ret_rank, *ret_row;
+  int64_t *n_dev;
+  uint8_t *xs, *h8;
+  uint16_t *gu;
+};
+
+static Arena ep_layer_tables(Arena a, int64_t tokens, int64_t hidden, int64_t inter, int experts, int topk, int world,
+                             int64_t cap, EpLayerTables &t) {
+  const int local = experts / world;
+  const int64_t rows = cap > 0 ? cap : 1;
+  const int keys = local > world ? local : world;
+  t.routes = a.take<float>((tokens > 0 ? tokens : 1) * 2 * topk);
+  t.xq = a.take<uint32_t>((tokens > 0 ? tokens : 1) * (stride_for(hidden) / 8 + 1));
+  t.slots = a.take<int>((tokens > 0 ? tokens : 1) * topk);
+  t.scratch = a.take<int>(sort_scratch_ints(keys));
+  t.n_dev = a.take<int64_t>(1);
+  t.xs_scales = a.take<float>(rows);
+  t.rmeta = a.take<float>(2 * rows);
+  t.ret_prob = a.take<float>(rows);
+  t.ret_rank = a.take<int>(rows);
+  t.ret_row = a.take<int>(rows);
+  t.offsets = a.take<int>(local + 1);
+  t.tiles = a.take<int>(1 + 2 * ((rows + 127) / 128 + local));
+  t.perm = a.take<int>(rows);
+  t.xs = a.take<uint8_t>(rows * hidden);
+  t.gu = a.take<uint16_t>(rows * 2 * inter);
+  t.hq = a.take<uint32_t>(rows * (inter / 8 + 1));
+  t.h8 = a.take<uint8_t>(rows * inter);
+  return a;
+}
+
+static int check_ep_layer(int64_t tokens, int64_t hidden, int64_t inter, int experts, int topk, int world,
+                          int64_t recv_cap) {
+  if (tokens < 0 || tokens > 1048576 || hidden % 256 || inter % 256 || hidden < 256 || inter < 256 ||
+      hidden > 32768 || inter > 32768 || !(topk > 0 && topk <= experts && experts <= 128 && topk <= 32) ||
+      world < 1 || world > kMaxRanks || experts % world || recv_cap < 0 || recv_cap > 32 * 1048576)
+    return set_err(CLEFQ_ERR_SHAPE, "unsupported expert-parallel MoE layer shape");
+  return 0;
+}
+
+int64_t clefq_moe_ep_layer_region_bytes(int64_t tokens, int64_t hidden, int topk, int world, int64_t recv_cap) {
+  if (check_ep_layer(tokens, hidden, 256, topk, topk, world, recv_cap)) return -1;
+  int *c;
+  uint32_t *r;
+  uint16_t *p;
+  return aligned_total(ep_region(Arena{nullptr, INT64_MAX}, tokens, hidden, topk, world, recv_cap, &c, &r, &p));
+}
+
+int64_t clefq_moe_ep_layer_workspace_size(int64_t tokens, int64_t hidden, int64_t inter, int experts, int topk,
+                                          int world, int64_t recv_cap) {
+  if (check_ep_layer(tokens, hidden, inter, experts, topk, world, recv_cap)) return -1;
+  EpLayerTables t;
+  return aligned_total(
+      ep_layer_tables(Arena{nullptr, INT64_MAX}, tokens, hidden, inter, experts, topk, world, recv_cap, t));
+}
+
+int clefq_moe_ep_layer(clefq_comm *c, void *stream, const void *x, const void *logits, int logits_dtype,
+                       int64_t tokens, int64_t hidden, int64_t inter, int experts, int topk, int64_t recv_cap,
+                       const void *gate_tiled, const float *gate_scales, const void *up_tiled,
+                       const float *up_scales, const void *down_tiled, const float *down_scales, void *out,
+                       float *routes_out, void *workspace, int64_t workspace_bytes) {
+  if (!clefq_comm_ready(c)) return set_err(CLEFQ_ERR_SHAPE, "expert-parallel layer: communicator peers not opened");
+  const int world = c->world, rank = c->rank;
+  int rc = check_ep_layer(tokens, hidden, inter, experts, topk, world, recv_cap);
+  if (rc) return rc;
+  if (logits_dtype != CLEFQ_BF16 && logits_dtype != CLEFQ_F32) return set_err(CLEFQ_ERR_SHAPE, "logits dtype");
+  if ((tokens > 0 && (!x || !logits || !out)) || (tokens > 0 && (!al16(x) || !al16(out))))
+    return set_err(CLEFQ_ERR_ALIGN, "x and out must be 16-byte aligned");
+  const int local = experts / world;
+  const int tile_rows = gemm_tile_rows((int)(2 * inter), (int)(inter / 128));
+  // hidden and intermediate are multiples of 256, so both expert GEMMs run the 2-SM kernel,
+  // whose epilogue holds the return path
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int *counts;
+  uint32_t *recv;
+  uint16_t *products;
+  Arena region = ep_region(Arena{c->base + kCommHeader, c->bytes}, tokens, hidden, topk, world, recv_cap, &counts,
+                           &recv, &products);
+  if (!region.ok) return set_err(CLEFQ_ERR_WORKSPACE, "communicator region too small for this MoE layer");
+  EpLayerTables t;
+  Arena a = ep_layer_tables(Arena{static_cast<uint8_t *>(workspace), workspace_bytes}, tokens, hidden, inter, experts,
+                            topk, world, recv_cap, t);
+  if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "expert-parallel layer workspace too small");
+  int *status = device_status_word();
+  if (!status) return cuda_err("status word");
+  auto at = [&](int g, const void *p) { return c->peer[g] + (static_cast<const uint8_t *>(p) - c->base); };
+  const int sms = device_sms();
+  const int code_words = (int)(hidden / 8);
+  const int64_t rec_words = clefq_moe_ep_record_bytes(hidden) / 4;
+  const int64_t sh = stride_for(hidden);
+  float *routes = routes_out ? routes_out : t.routes;
+  int *my_counts = counts + rank * world;
+  // 1. route and pack this rank's tokens; plan: routes grouped by destination rank
+  if (tokens > 0) {
+    rc = launch_route(logits, logits_dtype == CLEFQ_F32, tokens, experts, topk, routes, s);
+    if (rc) return cuda_err("route launch");
+    rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, tokens, hidden, sh, t.xq, nullptr, 0, nullptr, 0);
+    if (rc) return rc;
+  }
+  SortArgs plan{};
+  plan.routes = routes;
+  plan.route_ld = 2 * topk;
+  plan.tokens = tokens;
+  plan.topk = topk;
+  plan.items = tokens * topk;
+  plan.key_div = local;
+  plan.keys = world;
+  plan.dedupe = false;
+  plan.hist = t.scratch;
+  plan.counts = my_counts;  // this rank's row of the matrix
+  plan.slots = t.slots;
+  if ((rc = launch_sort(plan, s))) return cuda_err("expert-parallel plan launch");
+  // 2. barrier: every rank's row of the counts matrix into every peer
+  CommBarrierArgs b = comm_barrier_args(c, status);
+  b.src = reinterpret_cast<const uint32_t *>(my_counts);
+  for (int g = 0; g < world; ++g) b.dst[g] = reinterpret_cast<uint32_t *>(at(g, my_counts));
+  b.words = world;
+  if ((rc = launch_comm_barrier(b, s))) return rc;
+  // 3. dispatch: records stored straight into the destination ranks' receive buffers
+  EpDispatchArgs d{};
+  d.xq = t.xq;
+  d.words_ld = sh / 8;
+  d.scales = reinterpret_cast<const float *>(t.xq + tokens * (sh / 8));
+  d.routes = routes;
+  d.slots = t.slots;
+  d.tokens = tokens;
+  d.topk = topk;
+  d.per_rank = local;
+  d.counts = counts;
+  d.rank = rank;
+  d.world = world;
+  d.code_words = code_words;
+  d.rec_words = rec_words;
+  for (int g = 0; g < world; ++g) d.recv[g] = reinterpret_cast<uint32_t *>(at(g, recv));
+  d.recv_cap = recv_cap;
+  d.err = status;
+  if ((rc = launch_ep_dispatch(d, s, sms))) return cuda_err("expert-parallel dispatch launch");
+  if ((rc = launch_comm_barrier(comm_barrier_args(c, status), s))) return rc;
+  // 4. the received routes: metadata, grouping by local expert, expert-sorted operand
+  EpReceiveArgs r{};
+  r.recv = recv;
+  r.counts = counts;
+  r.rank = rank;
+  r.world = world;
+  r.code_words = code_words;
+  r.rec_words = rec_words;
+  r.recv_cap = recv_cap;
+  r.expert_base = rank * local;
+  r.local_experts = local;
+  r.scales = t.xs_scales;
+  r.routes = t.rmeta;
+  r.ret_rank = t.ret_rank;
+  r.ret_row = t.ret_row;
+  r.ret_prob = t.ret_prob;
+  r.n_dev = t.n_dev;
+  r.err = status;
+  if ((rc = launch_ep_receive(r, s, sms))) return cuda_err("expert-parallel receive launch");
+  SortArgs grp{};
+  grp.routes = t.rmeta;
+  grp.route_ld = 2;
+  grp.tokens = recv_cap;
+  grp.topk = 1;
+  grp.items = recv_cap;
+  grp.items_dev = t.n_dev;
+  grp.key_div = 1;
+  grp.keys = local;
+  grp.dedupe = false;
+  grp.hist = t.scratch;
+  grp.offsets = t.offsets;
+  grp.tile_list = t.tiles;
+  grp.tile_rows = tile_rows;
+  grp.perm = t.perm;
+  if ((rc = launch_sort(grp, s))) return cuda_err("expert-parallel grouping launch");
+  if (recv_cap > 0 && launch_gather_unpack_i4(recv, rec_words, t.perm, 1, recv_cap, (int)hidden, t.xs, hidden, s, sms,
+                                              t.n_dev))
+    return cuda_err("expert-parallel gather launch");
+  // 5. expert FFN; the down-GEMM epilogue stores bf16(value * probability) at the home
+  //    rank's product row
+  if (recv_cap > 0) {
+    ExpertReturn ret{};
+    ret.rows_dev = t.n_dev;
+    for (int g = 0; g < world; ++g) ret.base[g] = reinterpret_cast<uint16_t *>(at(g, products));
+    ret.rank = t.ret_rank;
+    ret.row = t.ret_row;
+    ret.prob = t.ret_prob;
+    rc = run_expert_ffn(s, t.xs, recv_cap, t.xs_scales, 1, t.tiles, t.offsets, t.perm, local, tile_rows, hidden,
+                        inter, gate_tiled, gate_scales, up_tiled, up_scales, down_tiled, down_scales, t.gu, t.hq,
+                        t.h8, nullptr, &ret);
+    if (rc) return rc;
+  }
+  // 6. barrier: every product is home; the reference's ascending-expert chain
+  if ((rc = launch_comm_barrier(comm_barrier_args(c, status), s))) return rc;
+  if (tokens > 0 && launch_combine(products, routes, nullptr, tokens, topk, hidden, static_cast<uint16_t *>(out), s,
+                                   sms, true))
+    return cuda_err("combine launch");
+  return 0;
 }
 
 // ---- tensor-parallel dense MLP --------------------------------------------------------

@@ -35,6 +35,9 @@ struct PrepareArgs {
   uint32_t *code_dst[kMaxRanks];
   int64_t code_ld;
   int n_code_dst;
+  // GEMM-input packing only: when set, only the first *rows_dev rows (<= rows) are packed;
+  // the storage layout still spans `rows`
+  const int64_t *rows_dev;
 };
 int launch_prepare(const PrepareArgs &a, cudaStream_t stream);
 int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);
@@ -77,6 +80,14 @@ struct GemmParams {
   // as from out), e.g. peers' symmetric buffers over NVLink
   uint16_t *out_peer[kMaxPeers];
   int n_out_peer;
+  // grouped 2-SM kernel only, expert-parallel return: output row r (a received route) is
+  // stored as bf16(value * ret_prob[r]) at ret_base[ret_rank[r]] + ret_row[r] * ldo (its
+  // home rank's product buffer, over NVLink for a peer) instead of at out
+  uint16_t *ret_base[kMaxRanks];
+  const int *ret_rank;
+  const int *ret_row;
+  const float *ret_prob;
+  int store16;              // set by launch_gemm: every output address allows 16-byte stores
 };
 int launch_gemm(const GemmParams &p, cudaStream_t stream);
 // Token rows per tile of the kernel launch_gemm picks for this output shape (grouped
@@ -149,6 +160,40 @@ struct SortArgs {
 };
 int64_t sort_scratch_ints(int keys);
 int launch_sort(SortArgs a, cudaStream_t stream);
+
+// Fused expert parallelism (ep.cu).
+constexpr int kSiteEpCapacity = 9;  // status site: more records than the receive capacity
+struct EpDispatchArgs {
+  const uint32_t *xq;        // packed token rows [tokens][words_ld]
+  int64_t words_ld;
+  const float *scales;       // [tokens]
+  const float *routes;       // [tokens][2 * topk]
+  const int *slots;          // send slot per route (grouped by destination rank)
+  int64_t tokens;
+  int topk, per_rank;
+  const int *counts;         // [world][world] in the symmetric region
+  int rank, world;
+  int code_words;
+  int64_t rec_words;
+  uint32_t *recv[kMaxRanks]; // every rank's receive buffer as mapped here
+  int64_t recv_cap;          // records each receive buffer holds
+  int *err;
+};
+struct EpReceiveArgs {
+  const uint32_t *recv;      // this rank's receive buffer
+  const int *counts;         // [world][world]
+  int rank, world;
+  int code_words;
+  int64_t rec_words, recv_cap;
+  int expert_base, local_experts;
+  float *scales, *routes;    // [cap], [cap][2]
+  int *ret_rank, *ret_row;
+  float *ret_prob;
+  int64_t *n_dev;
+  int *err;
+};
+int launch_ep_dispatch(const EpDispatchArgs &a, cudaStream_t stream, int num_sms);
+int launch_ep_receive(const EpReceiveArgs &a, cudaStream_t stream, int num_sms);
 
 int device_sms();
 int report_error(int code, const char *msg);  // sets clefq_last_error()

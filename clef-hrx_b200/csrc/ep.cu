@@ -177,4 +177,97 @@ int launch_ep_combine(const uint16_t *products, const int *slots, const float *r
   return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
 }
 
+
+// ---- fused expert parallelism over symmetric NVLink buffers ------------------------------
+// counts: the G x G matrix in the symmetric region, row s = routes rank s sends to each rank
+// (every row is complete once the first barrier of the layer has passed).
+
+// One warp per route: the record goes straight into its destination rank's receive buffer:
+// position = (records the lower ranks send to that rank) + (this route's place among the
+// routes this rank sends there).  Record: code words, f32 scale, global expert id,
+// probability, home route index t * topk + k.
+__global__ void ep_dispatch_kernel(EpDispatchArgs a) {
+  __shared__ int s_send[kMaxRanks], s_recv[kMaxRanks];
+  if (threadIdx.x < (unsigned)a.world) {
+    const int g = threadIdx.x;
+    int so = 0, ro = 0;
+    for (int d = 0; d < g; ++d) so += a.counts[a.rank * a.world + d];
+    for (int src = 0; src < a.rank; ++src) ro += a.counts[src * a.world + g];
+    s_send[g] = so;
+    s_recv[g] = ro;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t total = a.tokens * a.topk;
+  const int64_t wstride = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t i = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); i < total; i += wstride) {
+    const int64_t t = i / a.topk;
+    const int r = (int)(i % a.topk);
+    const int e = (int)a.routes[t * 2 * a.topk + r];
+    const int d = e >= 0 ? e / a.per_rank : a.world;
+    if (d >= a.world) continue;
+    const int64_t pos = (int64_t)s_recv[d] + (a.slots[i] - s_send[d]);
+    if (pos < 0 || pos >= a.recv_cap) {
+      if (lane == 0) atomicCAS(a.err, 0, kSiteEpCapacity);
+      continue;
+    }
+    uint32_t *rec = a.recv[d] + pos * a.rec_words;
+    const uint32_t *src = a.xq + t * a.words_ld;
+    for (int w = lane * 4; w < a.code_words; w += 128)
+      *reinterpret_cast<uint4 *>(rec + w) = *reinterpret_cast<const uint4 *>(src + w);
+    if (lane == 0)
+      *reinterpret_cast<uint4 *>(rec + a.code_words) =
+          make_uint4(__float_as_uint(a.scales[t]), (uint32_t)e,
+                     __float_as_uint(a.routes[t * 2 * a.topk + a.topk + r]), (uint32_t)i);
+  }
+}
+
+// Received records -> per-record activation scale, (local expert, probability) route rows,
+// and where the product goes back: home rank (from the record's position) and home route.
+// n_dev = records received (the matrix column of this rank).
+__global__ void ep_receive_kernel(EpReceiveArgs a) {
+  __shared__ int s_off[kMaxRanks + 1];
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int src = 0; src < a.world; ++src) {
+      s_off[src] = run;
+      run += a.counts[src * a.world + a.rank];
+    }
+    s_off[a.world] = run;
+    if (blockIdx.x == 0) {
+      *a.n_dev = run < a.recv_cap ? run : a.recv_cap;
+      if (run > a.recv_cap) atomicCAS(a.err, 0, kSiteEpCapacity);
+    }
+  }
+  __syncthreads();
+  const int64_t n = s_off[a.world] < a.recv_cap ? s_off[a.world] : a.recv_cap;
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < n; p += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 meta = *reinterpret_cast<const uint4 *>(a.recv + p * a.rec_words + a.code_words);
+    const int e = (int)meta.y - a.expert_base;
+    int src = 0;
+    while (src + 1 < a.world && s_off[src + 1] <= p) ++src;
+    a.scales[p] = __uint_as_float(meta.x);
+    a.routes[2 * p] = (float)(e >= 0 && e < a.local_experts ? e : -1);
+    a.routes[2 * p + 1] = __uint_as_float(meta.z);
+    a.ret_prob[p] = __uint_as_float(meta.z);
+    a.ret_rank[p] = src;
+    a.ret_row[p] = (int)meta.w;
+  }
+}
+
+int launch_ep_dispatch(const EpDispatchArgs &a, cudaStream_t stream, int num_sms) {
+  const int64_t total = a.tokens * a.topk;
+  if (total == 0) return 0;
+  int64_t blocks = (total + 7) / 8, cap = (int64_t)num_sms * 16;
+  ep_dispatch_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+}
+
+int launch_ep_receive(const EpReceiveArgs &a, cudaStream_t stream, int num_sms) {
+  int64_t blocks = (a.recv_cap + 255) / 256, cap = (int64_t)num_sms * 8;
+  if (blocks < 1) blocks = 1;
+  ep_receive_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+}
+
 }  // namespace cq

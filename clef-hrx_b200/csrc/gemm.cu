@@ -452,7 +452,20 @@ static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, 
 bool gemm_uses_pairs(const GemmParams &p) { return p.n_split % 2 == 0 && p.n % 256 == 0; }
 int gemm_tile_rows(int n, int n_split) { return (n_split % 2 == 0 && n % 256 == 0) ? two_sm::BN2 : BN; }
 
-int launch_gemm(const GemmParams &p, cudaStream_t stream) {
+static bool allows_store16(const GemmParams &p) {
+  auto al = [](const void *q) { return ((uintptr_t)q & 15) == 0; };
+  if (p.ldo % 8 || (p.out && !al(p.out)) || (p.residual && (!al(p.residual) || p.ldr % 8))) return false;
+  for (int d = 0; d < p.n_out_peer; ++d)
+    if (!al(p.out_peer[d])) return false;
+  if (p.ret_row)
+    for (int g = 0; g < kMaxRanks; ++g)
+      if (!al(p.ret_base[g])) return false;
+  return true;
+}
+
+int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
+  GemmParams p = p0;
+  p.store16 = allows_store16(p);
   if (p.n % BM || p.k % 256 || p.k <= 0 || p.n <= 0) return CLEFQ_ERR_SHAPE;
   if (!(p.bits == 4 || p.bits == 8)) return CLEFQ_ERR_SHAPE;
   if ((uintptr_t)p.a_op % 16 || p.a_ld % 16 || p.a_ld < p.k) return CLEFQ_ERR_ALIGN;
@@ -464,6 +477,7 @@ int launch_gemm(const GemmParams &p, cudaStream_t stream) {
   if (p.residual && ((uintptr_t)p.residual % 8 || p.ldr % 4)) return CLEFQ_ERR_ALIGN;
   const bool pairs = gemm_uses_pairs(p);
   if (p.n_out_peer && (!pairs || p.grouped || !p.out || p.n_out_peer > kMaxPeers)) return CLEFQ_ERR_SHAPE;
+  if (p.ret_row && (!pairs || !p.grouped || !p.scatter || !p.ret_rank || !p.ret_prob)) return CLEFQ_ERR_SHAPE;
   for (int d = 0; d < p.n_out_peer; ++d)
     if ((uintptr_t)p.out_peer[d] % 8) return CLEFQ_ERR_ALIGN;
   const int tile_rows = pairs ? two_sm::BN2 : BN;

@@ -79,6 +79,52 @@ struct TileMap2 {
   }
 };
 
+template <int V> struct StoreVec;
+template <> struct StoreVec<4> { using T = uint2; };
+template <> struct StoreVec<8> { using T = uint4; };
+
+// Stores token rows [m_begin, m_end) of a CTA's staged BF16 tile (128 columns from col0):
+// V columns per lane, so 128 / V lanes per row (V = 8: 16-byte stores, two rows per warp
+// instruction).  Dense: optional residual bf16(res + y), and copies to out_peer.  Grouped:
+// row scatter through perm, or the expert-parallel return bf16(value * probability) into
+// the route's home rank.
+template <bool GROUPED, int V>
+CQ_DEV void store_tile_rows(const GemmParams &p, const uint16_t *staging, int64_t row0, int rows_valid, int col0,
+                            int m_begin, int m_end, int lane) {
+  using Vec = typename StoreVec<V>::T;
+  constexpr int LPR = 128 / V;  // lanes per row
+  constexpr int RPI = 32 / LPR;  // rows per warp iteration
+  const int sub = lane / LPR, l = lane % LPR;
+  for (int m = m_begin + sub; m < m_end && m < rows_valid; m += RPI) {
+    const int64_t pos = row0 + m;
+    int64_t orow = pos;
+    if (GROUPED && p.scatter) orow = p.perm[pos];
+    Vec v = *reinterpret_cast<const Vec *>(staging + m * 128 + V * l);
+    uint16_t *hv = reinterpret_cast<uint16_t *>(&v);
+    if (!GROUPED && p.residual) {
+      const Vec rv = *reinterpret_cast<const Vec *>(p.residual + pos * p.ldr + col0 + V * l);
+      const uint16_t *hr = reinterpret_cast<const uint16_t *>(&rv);
+#pragma unroll
+      for (int q = 0; q < V; ++q) hv[q] = f32_to_bf16(__fadd_rn(bf16_to_f32(hr[q]), bf16_to_f32(hv[q])));
+    }
+    if (GROUPED && p.ret_row) {
+      const float pr = p.ret_prob[orow];
+#pragma unroll
+      for (int q = 0; q < V; ++q) hv[q] = f32_to_bf16(__fmul_rn(bf16_to_f32(hv[q]), pr));
+      uint16_t *dst = p.ret_base[p.ret_rank[orow]] + (int64_t)p.ret_row[orow] * p.ldo + col0 + V * l;
+      *reinterpret_cast<Vec *>(dst) = v;
+      continue;
+    }
+    const int64_t off = orow * p.ldo + col0 + V * l;
+    *reinterpret_cast<Vec *>(p.out + off) = v;
+    if (!GROUPED && p.n_out_peer) {
+#pragma unroll
+      for (int d = 0; d < kMaxPeers; ++d)
+        if (d < p.n_out_peer) *reinterpret_cast<Vec *>(p.out_peer[d] + off) = v;
+    }
+  }
+}
+
 template <bool GROUPED, int BITS>
 __global__ void __launch_bounds__(THREADS2, 1)
     gemm_i8_2sm_kernel(const __grid_constant__ CUtensorMap tok_map, const __grid_constant__ CUtensorMap w_map0,
@@ -362,29 +408,9 @@ __global__ void __launch_bounds__(THREADS2, 1)
       if (GROUPED || !p.out_f32) {
         named_barrier_sync(1, 32 * EPI_WARPS);
         // each warp stores 24 token rows, 256 contiguous bytes per row
-        const int m_end = eidx * (BN2 / EPI_WARPS) + BN2 / EPI_WARPS;
-        for (int m = eidx * (BN2 / EPI_WARPS); m < m_end && m < rows_valid; ++m) {
-          const int64_t pos = row0 + m;
-          int64_t orow = pos;
-          if (GROUPED && p.scatter) orow = p.perm[pos];
-          uint2 v = *reinterpret_cast<const uint2 *>(staging + m * 128 + 4 * lane);
-          if (!GROUPED && p.residual) {
-            const uint2 rv = *reinterpret_cast<const uint2 *>(p.residual + pos * p.ldr + col0 + 4 * lane);
-            const uint16_t *hv = reinterpret_cast<const uint16_t *>(&v);
-            const uint16_t *hr = reinterpret_cast<const uint16_t *>(&rv);
-            uint16_t o4[4];
-#pragma unroll
-            for (int qq = 0; qq < 4; ++qq) o4[qq] = f32_to_bf16(__fadd_rn(bf16_to_f32(hr[qq]), bf16_to_f32(hv[qq])));
-            v = *reinterpret_cast<uint2 *>(o4);
-          }
-          const int64_t off = orow * p.ldo + col0 + 4 * lane;
-          *reinterpret_cast<uint2 *>(p.out + off) = v;
-          if (!GROUPED && p.n_out_peer) {
-#pragma unroll
-            for (int d = 0; d < kMaxPeers; ++d)
-              if (d < p.n_out_peer) *reinterpret_cast<uint2 *>(p.out_peer[d] + off) = v;
-          }
-        }
+        const int m0 = eidx * (BN2 / EPI_WARPS);
+        if (p.store16) store_tile_rows<GROUPED, 8>(p, staging, row0, rows_valid, col0, m0, m0 + BN2 / EPI_WARPS, lane);
+        else store_tile_rows<GROUPED, 4>(p, staging, row0, rows_valid, col0, m0, m0 + BN2 / EPI_WARPS, lane);
         named_barrier_sync(1, 32 * EPI_WARPS);
       }
     }

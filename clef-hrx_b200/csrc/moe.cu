@@ -446,9 +446,11 @@ int launch_gather(const uint8_t *src, int64_t src_ld, const int *perm, int div, 
 // Weighted combine in ascending expert order with BF16 rounding at every step; eight
 // columns per thread.  order == nullptr: find the ascending order per token like
 // omni_combine.loom (prev/best scan).
+// weighted: values already hold bf16(v * p) (the expert-parallel products), so only the
+// chain's additions remain.
 __global__ void combine_kernel(const uint16_t *__restrict__ values, const float *__restrict__ routes,
                                const float *__restrict__ order, int64_t tokens, int topk, int64_t width,
-                               uint16_t *__restrict__ out) {
+                               uint16_t *__restrict__ out, bool weighted) {
   const int64_t per_tok = width / 8;
   const int64_t total = tokens * per_tok;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -480,7 +482,8 @@ __global__ void combine_kernel(const uint16_t *__restrict__ values, const float 
       const uint4 raw = *reinterpret_cast<const uint4 *>(values + (t * topk + r) * width + c);
       const uint16_t *h = reinterpret_cast<const uint16_t *>(&raw);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) s[q] = bf16r(__fadd_rn(s[q], bf16r(__fmul_rn(bf16_to_f32(h[q]), p))));
+      for (int q = 0; q < 8; ++q)
+        s[q] = bf16r(__fadd_rn(s[q], weighted ? bf16_to_f32(h[q]) : bf16r(__fmul_rn(bf16_to_f32(h[q]), p))));
     }
     uint4 o;
     uint16_t *oh = reinterpret_cast<uint16_t *>(&o);
@@ -501,7 +504,7 @@ CQ_DEV void bf16r2_inplace(float &lo, float &hi) {
 // The same combine with topk fixed at compile time: the K route rows' 16-byte chunks are all
 // loaded before the ordered chain consumes them, so a thread has K loads in flight instead
 // of one.  Identical arithmetic and order to combine_kernel.
-template <int K>
+template <int K, bool WEIGHTED>
 __global__ void combine_k_kernel(const uint16_t *__restrict__ values, const float *__restrict__ routes,
                                  const float *__restrict__ order, int64_t tokens, int64_t width,
                                  uint16_t *__restrict__ out) {
@@ -551,9 +554,13 @@ __global__ void combine_k_kernel(const uint16_t *__restrict__ values, const floa
       const uint32_t *hw = reinterpret_cast<const uint32_t *>(&raw[j]);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        float lo = __fmul_rn(__uint_as_float(hw[q] << 16), p);
-        float hi = __fmul_rn(__uint_as_float(hw[q] & 0xffff0000u), p);
-        bf16r2_inplace(lo, hi);
+        float lo = __uint_as_float(hw[q] << 16);
+        float hi = __uint_as_float(hw[q] & 0xffff0000u);
+        if (!WEIGHTED) {
+          lo = __fmul_rn(lo, p);
+          hi = __fmul_rn(hi, p);
+          bf16r2_inplace(lo, hi);
+        }
         lo = __fadd_rn(s[2 * q], lo);
         hi = __fadd_rn(s[2 * q + 1], hi);
         bf16r2_inplace(lo, hi);
@@ -571,27 +578,36 @@ __global__ void combine_k_kernel(const uint16_t *__restrict__ values, const floa
 }
 
 int launch_combine(const uint16_t *values, const float *routes, const float *order, int64_t tokens, int topk,
-                   int64_t width, uint16_t *out, cudaStream_t stream, int num_sms) {
+                   int64_t width, uint16_t *out, cudaStream_t stream, int num_sms, bool weighted) {
   if (width % 8) return CLEFQ_ERR_SHAPE;
   if ((uintptr_t)values % 16 || (uintptr_t)out % 16) return CLEFQ_ERR_ALIGN;
   const int64_t total = tokens * (width / 8);
   if (total == 0) return 0;
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
+#define CQ_COMBINE_K(K)                                                                            \
+  (weighted ? combine_k_kernel<K, true><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out) \
+            : combine_k_kernel<K, false><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out))
   switch (topk) {
-    case 8: combine_k_kernel<8><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out); break;
-    case 4: combine_k_kernel<4><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out); break;
-    case 2: combine_k_kernel<2><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out); break;
-    default: combine_kernel<<<grid, 256, 0, stream>>>(values, routes, order, tokens, topk, width, out); break;
+    case 8: CQ_COMBINE_K(8); break;
+    case 4: CQ_COMBINE_K(4); break;
+    case 2: CQ_COMBINE_K(2); break;
+    default: combine_kernel<<<grid, 256, 0, stream>>>(values, routes, order, tokens, topk, width, out, weighted); break;
   }
+#undef CQ_COMBINE_K
   return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
 }
 
 
 // dst[p][:] = s8 operand of packed int4 row perm[p] / div (unpack fused with the gather).
 __global__ void gather_unpack_i4_kernel(const uint32_t *__restrict__ a, int64_t a_ld, const int *__restrict__ perm,
-                                        int div, int64_t rows, int k, uint8_t *__restrict__ dst, int64_t dst_ld) {
+                                        int div, int64_t rows, const int64_t *rows_dev, int k,
+                                        uint8_t *__restrict__ dst, int64_t dst_ld) {
   const int groups = k / 32;
+  if (rows_dev) {
+    const int64_t d = *rows_dev;
+    rows = d < 0 ? 0 : (d < rows ? d : rows);
+  }
   const int64_t total = rows * groups;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t p = i / groups;
@@ -611,13 +627,13 @@ __global__ void gather_unpack_i4_kernel(const uint32_t *__restrict__ a, int64_t 
 }
 
 int launch_gather_unpack_i4(const uint32_t *a, int64_t a_ld, const int *perm, int div, int64_t rows, int k,
-                            uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms) {
+                            uint8_t *dst, int64_t dst_ld, cudaStream_t stream, int num_sms, const int64_t *rows_dev) {
   const int64_t total = rows * (k / 32);
   if (total <= 0) return 0;
   if ((uintptr_t)dst % 16 || dst_ld % 16) return CLEFQ_ERR_ALIGN;
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
-  gather_unpack_i4_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(a, a_ld, perm, div, rows, k,
-                                                                                       dst, dst_ld);
+  gather_unpack_i4_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(a, a_ld, perm, div, rows,
+                                                                                       rows_dev, k, dst, dst_ld);
   return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
 }
 

@@ -481,7 +481,14 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
   const int words = p.stride >> 3;
   const int code_words = p.width >> 3;
   const int q = lane >> 3, r = lane & 7;
-  const int64_t nblk = (p.rows + rpb - 1) / rpb;
+  // rows to pack: p.rows, or fewer when the count is only known on the device (the code
+  // and scale layout always spans p.rows)
+  int64_t nrows = p.rows;
+  if (p.rows_dev) {
+    const int64_t d = *p.rows_dev;
+    nrows = d < 0 ? 0 : (d < p.rows ? d : p.rows);
+  }
+  const int64_t nblk = (nrows + rpb - 1) / rpb;
   const uint32_t stage0 = smem_u32(smem + (TAB ? kSiluEntries * 2 : 0) + kPackRedBytes);
   const uint32_t chunk = blockDim.x * 16;                    // one 16-byte chunk per thread
   const uint32_t stage_bytes = (uint32_t)(NS * NOP * 4) * chunk;
@@ -491,7 +498,7 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
 
   auto issue = [&](int64_t b, int stg) {
     const int64_t row = b * rpb + team;
-    const bool ok = b < nblk && row < p.rows;
+    const bool ok = b < nblk && row < nrows;
     const uint32_t base = stage0 + stg * stage_bytes + threadIdx.x * 16;
 #pragma unroll
     for (int sl = 0; sl < NS; ++sl) {
@@ -521,7 +528,7 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
   int par = 0, st = 0;
   for (; blk < nblk; blk += gridDim.x, par ^= 1) {
     const int64_t row = blk * rpb + team;
-    const bool row_ok = row < p.rows;
+    const bool row_ok = row < nrows;
     cp_async_wait_dyn(nstg - 1);  // this block's copies (all but the nstg-1 newest groups)
     const uint32_t base = stage0 + st * stage_bytes + threadIdx.x * 16;
     float v[NS][32];
@@ -736,16 +743,20 @@ int launch_prepare(const PrepareArgs &a0, cudaStream_t stream) {
                           (a.x_ld & 7) == 0 && (a.mode != MODE_SWIGLU || (a.aux_ld & 7) == 0);
   // The table pays for its 128 KB shared-memory fill once a launch has about a full
   // wave of groups to process; small launches evaluate the activation directly.
-  // Extra code destinations exist only in the GEMM-input kernel, so they take the table at
-  // any size.
-  const bool tab = gemm_input && a.mode == MODE_SWIGLU && (a.rows * (int64_t)ngroups >= 2048 || a.n_code_dst);
+  // Extra code destinations and device row counts exist only in the GEMM-input kernel, so
+  // they take the table at any size.
+  const bool tab = gemm_input && a.mode == MODE_SWIGLU &&
+                   (a.rows * (int64_t)ngroups >= 2048 || a.n_code_dst || a.rows_dev);
   if (a.n_code_dst && !tab)
     return report_error(CLEFQ_ERR_SHAPE, "prepare: extra code destinations are for SwiGLU GEMM-input packing");
+  if (a.rows_dev && !(gemm_input && (a.mode == MODE_PLAIN || tab)))
+    return report_error(CLEFQ_ERR_SHAPE, "prepare: a device row count needs the GEMM-input kernel");
   if (gemm_input && (a.mode == MODE_PLAIN || tab) && try_launch_pack(a, tab, stream)) {
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : report_error(CLEFQ_ERR_CUDA, cudaGetErrorString(e));
   }
-  if (a.n_code_dst) return report_error(CLEFQ_ERR_SHAPE, "prepare: extra code destinations need the GEMM-input kernel");
+  if (a.n_code_dst || a.rows_dev)
+    return report_error(CLEFQ_ERR_SHAPE, "prepare: this launch shape needs the GEMM-input kernel");
   int tw, ch;
   if (norm) {
     tw = 8;  // the reference's 256-thread reduction order

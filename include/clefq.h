@@ -347,6 +347,36 @@ CLEFQ_API int clefq_tp_mlp(clefq_comm *comm, void *stream, const void *x, int64_
                            const void *residual, void *out, void *workspace, int64_t workspace_bytes);
 CLEFQ_API void *clefq_tp_mlp_output(clefq_comm *comm, int64_t m, int64_t hidden, int64_t inter);
 
+/*
+ * Expert-parallel Omni MoE layer with its exchanges inside the kernels (the reference's MoE
+ * block, src/omni.rs:761-857, with the experts split over the communicator's ranks: rank r
+ * owns experts [r*E/G, (r+1)*E/G) and passes their tiled weights, in clefq_moe's layout for
+ * E/G experts).  Every rank passes its own tokens; out [tokens][hidden] is bit-identical to
+ * clefq_moe over those tokens on one GPU.  No host synchronisation:
+ *   1. route and pack the tokens; group the routes by destination rank
+ *   2. barrier that also stores this rank's per-destination counts into every peer
+ *   3. dispatch: one record per route stored straight into the destination's receive buffer
+ *      (int4 code row, scale, expert id, probability, home route index); barrier
+ *   4. the received routes grouped by local expert; grouped gate|up GEMM, SwiGLU packing and
+ *      down GEMM, whose epilogue stores bf16(value * probability) into the home rank's
+ *      product buffer at the route's index; barrier
+ *   5. the reference's ascending-expert BF16 chain over the returned products
+ * recv_cap bounds the records one rank receives (the same on every rank; world*tokens*topk
+ * always suffices); exceeding it records status site 9 (clefq_status -> CLEFQ_ERR_TIMEOUT
+ * class error) and drops the excess.  Region and workspace sizes from the two queries (-1
+ * for an unsupported shape).
+ */
+CLEFQ_API int64_t clefq_moe_ep_layer_region_bytes(int64_t tokens, int64_t hidden, int topk, int world,
+                                                  int64_t recv_cap);
+CLEFQ_API int64_t clefq_moe_ep_layer_workspace_size(int64_t tokens, int64_t hidden, int64_t inter, int experts,
+                                                    int topk, int world, int64_t recv_cap);
+CLEFQ_API int clefq_moe_ep_layer(clefq_comm *comm, void *stream, const void *x, const void *logits,
+                                 int logits_dtype, int64_t tokens, int64_t hidden, int64_t inter, int experts,
+                                 int topk, int64_t recv_cap, const void *gate_tiled, const float *gate_scales,
+                                 const void *up_tiled, const float *up_scales, const void *down_tiled,
+                                 const float *down_scales, void *out, float *routes_out, void *workspace,
+                                 int64_t workspace_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -188,3 +188,92 @@ def test_ep_two_ranks_nccl():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     mp.start_processes(_nccl_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
+
+
+# ---------------------------------------------------------------------------------------
+# fused path: clefq_moe_ep_layer over a Comm (records and products stored into peers)
+# ---------------------------------------------------------------------------------------
+@pytest.mark.gpu
+@pytest.mark.parametrize("experts,topk,tokens", [(16, 4, 100), (128, 8, 300), (32, 8, 1)])
+def test_ep_fused_one_rank_matches_moe(cq, experts, topk, tokens):
+    from clefq.comm import Comm
+    from clefq.ep import ep_layer_region_bytes, omni_moe_ep_fused, shard_experts
+    hidden, inter = 512, 256
+    gate, up, down = _weights(cq, experts, inter, hidden, 17)
+    shard = shard_experts(gate, up, down, experts, inter, hidden, 0, 1)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(tokens)
+    with Comm(ep_layer_region_bytes(tokens, hidden, topk, 1, tokens * topk)) as comm:
+        for rep in range(3):   # barrier epochs and buffers reused across calls
+            x = torch.randn(tokens, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+            logits = torch.randn(tokens, experts, device="cuda", generator=gen).to(torch.bfloat16)
+            out, routes = omni_moe_ep_fused(x, logits, shard, comm, topk)
+            ref_routes = torch.empty(tokens, 2 * topk, dtype=torch.float32, device="cuda")
+            ref = cq.omni_moe(x, logits, gate, up, down, experts=experts, topk=topk, routes_out=ref_routes)
+            assert torch.equal(routes, ref_routes)
+            assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), f"call {rep}"
+        cq.status()
+
+
+@pytest.mark.gpu
+def test_ep_fused_capacity_overflow_is_reported(cq):
+    """A receive capacity below the routes present: the excess records are dropped, the
+    status reports it on the host, and the device keeps working."""
+    from clefq.comm import Comm
+    from clefq.ep import ep_layer_region_bytes, omni_moe_ep_fused, shard_experts
+    experts, topk, hidden, inter, tokens = 16, 4, 512, 256, 64
+    gate, up, down = _weights(cq, experts, inter, hidden, 3)
+    shard = shard_experts(gate, up, down, experts, inter, hidden, 0, 1)
+    x = torch.randn(tokens, hidden, device="cuda").to(torch.bfloat16)
+    logits = torch.randn(tokens, experts, device="cuda").to(torch.bfloat16)
+    cap = tokens * topk // 2
+    with Comm(ep_layer_region_bytes(tokens, hidden, topk, 1, cap)) as comm:
+        omni_moe_ep_fused(x, logits, shard, comm, topk, recv_cap=cap)
+        with pytest.raises(RuntimeError, match="gave up"):
+            cq.status()
+        out, _ = omni_moe_ep_fused(x, logits, shard, comm, topk, recv_cap=cap)
+        with pytest.raises(RuntimeError):
+            cq.status()
+    ref = cq.omni_moe(x, logits, gate, up, down, experts=experts, topk=topk)
+    assert ref.shape == out.shape
+    cq.status()
+
+
+def _nccl_fused_worker(rank, world, port):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
+    import clefq as cq
+    from clefq.comm import Comm
+    from clefq.ep import ep_layer_region_bytes, omni_moe_ep_fused, shard_experts
+    torch.cuda.set_device(rank)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        experts, topk, hidden, inter = 32, 8, 512, 256
+        most = 257 + 31 * (world - 1)
+        cap = world * most * topk                   # the same on every rank
+        gate, up, down = _weights(cq, experts, inter, hidden, 5)
+        shard = shard_experts(gate, up, down, experts, inter, hidden, rank, world)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(1000 + rank)
+        with Comm(ep_layer_region_bytes(most, hidden, topk, world, cap)) as comm:
+            for rep in range(3):
+                tokens = 257 + 31 * rank - 100 * rep   # ranks and calls differ in token count
+                x = torch.randn(tokens, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+                logits = torch.randn(tokens, experts, device="cuda", generator=gen).to(torch.bfloat16)
+                out, routes = omni_moe_ep_fused(x, logits, shard, comm, topk, recv_cap=cap)
+                ref = cq.omni_moe(x, logits, gate, up, down, experts=experts, topk=topk)
+                assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), f"rank {rank} call {rep}"
+            cq.status()
+            dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_fused_ranks(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_nccl_fused_worker, args=(world, _free_port()), nprocs=world, join=True, start_method="spawn")
