@@ -46,7 +46,8 @@ _SYMBOLS = {
     "clefq_mlp_workspace_size": (ctypes.c_int64, ["l", "l", "l"]),
     "clefq_mlp": (ctypes.c_int, ["p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "p", "l"]),
     "clefq_mlp_host_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i"]),
-    "clefq_mlp_host": (ctypes.c_int, ["p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "l", "p", "l"]),
+    "clefq_mlp_host": (ctypes.c_int, ["p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "l", "i", "p",
+                                      "p", "l"]),
     "clefq_moe_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i", "i"]),
     "clefq_moe": (ctypes.c_int, ["p", "p", "p", "i", "l", "l", "l", "i", "i", "p", "p", "p", "p", "p", "p", "p", "p",
                                  "p", "l"]),
@@ -274,12 +275,18 @@ def mlp(x, gate: QuantizedWeight, up: QuantizedWeight, down: QuantizedWeight, re
     return out
 
 
+HOST_STREAMING = 1
+
+
 def mlp_host(x, gate: QuantizedWeight, up: QuantizedWeight, down: QuantizedWeight, residual=None, out=None,
-             chunk_rows=1024, workspace=None, sync=True):
+             chunk_rows=1024, workspace=None, sync=True, streaming=False, done_event=None):
     """The MLP block from host rows to host rows (clefq_mlp_host): row chunks stream through
     the GPU with their PCIe copies overlapping the neighbouring chunks' kernels.  x, residual
     and out are CPU bf16 [m][hidden] (pinned memory for overlap).  With sync=False the call
-    returns once enqueued on the current stream; out is ready when the stream reaches it."""
+    returns once enqueued; out is ready when the current stream reaches it, or when
+    done_event (a torch.cuda.Event) fires if one is given.  streaming=True lets the input
+    copies start before earlier work on the stream ends, so back-to-back calls overlap (the
+    workspace must then serve only these calls)."""
     if x.is_cuda or (residual is not None and residual.is_cuda):
         raise ValueError("mlp_host takes host tensors")
     m, hidden = x.shape
@@ -297,10 +304,17 @@ def mlp_host(x, gate: QuantizedWeight, up: QuantizedWeight, down: QuantizedWeigh
         raise ValueError("unsupported MLP shape")
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=gate.codes.device)
+    ev = None
+    if done_event is not None:
+        if not done_event.cuda_event:
+            done_event.record()  # torch creates the CUDA event at its first record
+        ev = ctypes.c_void_p(done_event.cuda_event)
     _call("clefq_mlp_host", _stream(), _ptr(x), m, hidden, inter, _ptr(gate.codes), _ptr(gate.scales), _ptr(up.codes),
           _ptr(up.scales), _ptr(down.codes), _ptr(down.scales), _ptr(residual), _ptr(out), chunk_rows,
-          _ptr(workspace), need)
+          HOST_STREAMING if streaming else 0, ev, _ptr(workspace), need)
     if sync:
+        if done_event is not None:
+            done_event.synchronize()
         torch.cuda.current_stream().synchronize()
     return out
 

@@ -205,15 +205,22 @@ CLEFQ_API int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, 
  * buffers [m][hidden] (pinned for the copies to overlap).  The rows run in chunks of
  * chunk_rows; each chunk's host->device copy, kernels and device->host copy overlap those of
  * its neighbours (library-owned copy streams).  Rows are independent, so the output equals
- * clefq_mlp's.  Ordered on `stream`: out is complete once the stream reaches that point.
+ * clefq_mlp's.
+ *   flags: CLEFQ_HOST_STREAMING lets this call's input copies start before earlier work on
+ *          `stream` finishes (the next call of a stream of calls then overlaps this one); the
+ *          workspace must then be used by these calls only.  0: the call starts after
+ *          earlier work on `stream`.
+ *   done_event: a cudaEvent_t recorded after the call's last output copy (out is complete
+ *          once it has fired); NULL makes `stream` wait for that copy instead.
  * workspace >= clefq_mlp_host_workspace_size(chunk_rows, hidden, inter, residual != NULL).
  */
+#define CLEFQ_HOST_STREAMING 1
 CLEFQ_API int64_t clefq_mlp_host_workspace_size(int64_t chunk_rows, int64_t hidden, int64_t inter, int with_residual);
 CLEFQ_API int clefq_mlp_host(void *stream, const void *x_host, int64_t m, int64_t hidden, int64_t inter,
                              const void *gate_tiled, const float *gate_scales, const void *up_tiled,
                              const float *up_scales, const void *down_tiled, const float *down_scales,
-                             const void *residual_host, void *out_host, int64_t chunk_rows, void *workspace,
-                             int64_t workspace_bytes);
+                             const void *residual_host, void *out_host, int64_t chunk_rows, int flags,
+                             void *done_event, void *workspace, int64_t workspace_bytes);
 
 /*
  * Omni INT4 MoE block; replaces the expert part of forward_layers_cached

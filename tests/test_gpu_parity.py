@@ -283,6 +283,16 @@ def test_mlp_block_host_chunks(cq, chunk, pinned, residual):
                           chunk_rows=chunk)
         assert not out.is_cuda
         assert np.array_equal(out.view(torch.int16).numpy().view(np.uint16), ref)
+    # a stream of calls (each call's input copies overlap the previous call's kernels)
+    outs, events = [], []
+    for _ in range(3):
+        ev = torch.cuda.Event()
+        outs.append(cq.mlp_host(host(x), ws[0][1], ws[1][1], ws[2][1], residual=None if res is None else host(res),
+                                chunk_rows=chunk, sync=False, streaming=True, done_event=ev))
+        events.append(ev)
+    for ev, out in zip(events, outs):
+        ev.synchronize()
+        assert np.array_equal(out.view(torch.int16).numpy().view(np.uint16), ref)
     cq.status()
 
 
