@@ -738,7 +738,10 @@ int launch_prepare(const PrepareArgs &a0, cudaStream_t stream) {
   const int ngroups = a.width >> 8;
   const bool norm = a.mode == MODE_NORM || a.mode == MODE_NORM_STORE;
   if (a.rows == 0) return 0;
-  const bool gemm_input = a.bits == 4 && (a.op8 != nullptr || a.rowmax_out != nullptr || a.n_code_dst > 0) &&
+  // int4 codes (plain, or with the operand / row maxima / extra code destinations) take the
+  // persistent packing kernels; everything else the general one
+  const bool gemm_input = a.bits == 4 &&
+                          (a.op8 != nullptr || a.rowmax_out != nullptr || a.n_code_dst > 0 || a.mode == MODE_PLAIN) &&
                           ((uintptr_t)a.out & 15) == 0 &&
                           (a.x_ld & 7) == 0 && (a.mode != MODE_SWIGLU || (a.aux_ld & 7) == 0);
   // The table pays for its 128 KB shared-memory fill once a launch has about a full

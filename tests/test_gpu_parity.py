@@ -74,6 +74,19 @@ def test_prepare_random_matches_oracle(cq, rows, width, bits):
     assert np.array_equal(p.storage.cpu().numpy().view(np.uint32), storage)
 
 
+@pytest.mark.parametrize("rows,width", [(1, 256), (7, 768), (300, 2048), (130, 4096), (65, 12288), (3, 32768)])
+def test_prepare_codes_only_matches_oracle(cq, rows, width):
+    """Plain int4 packing without the s8 operand (weights, expert-parallel tokens) takes the
+    persistent packing kernel where it fits; codes, stride padding and scales stay exact."""
+    rng = np.random.default_rng(rows * 3 + width)
+    x = bf16_normal(rng, (rows, width), 1.7)
+    x[0, 5] = 0x7FC0
+    stride = o.stride_for(width)
+    p = cq.prepare(to_dev_bf16(x), 4, stride, operand=False)
+    storage, _, _, _ = o.prepare(x, 4, stride)
+    assert np.array_equal(p.storage.cpu().numpy().view(np.uint32), storage)
+
+
 def _gate_like(rng, rows, width):
     """SwiGLU/attention gate inputs with the reference test's exceptional rows
     (src/quantized.rs:1187-1266): 0, NaN, Inf, bf16 MAX, subnormal, +-80, formula."""
