@@ -383,8 +383,15 @@ def run_clefq(args, world, rank, local):
         if world > 1:
             ecomm.close()
         ops = 2.0 * MOE_T * MOE_K * (MOE_H * 2 * MOE_I + MOE_I * MOE_H)
+        moe_roof = None
+        if world > 1:
+            rec_b = clefq.lib().clefq_moe_ep_record_bytes(MOE_H)
+            link = (world - 1) / world * MOE_T * MOE_K * (rec_b + 2 * MOE_H)   # records out, products back
+            target = max(ops / (i8_peak * 1e12), link / 770e9) * 1e3
+            moe_roof = {"target_ms": target, "frac": target / mms, "int_ops_per_rank": ops,
+                        "nvlink_bytes_per_rank": link}
         moe = {"workload": "C4 Omni INT4 MoE layer: 8192 tokens per GPU, hidden 2048, 128 experts x (gate|up "
-                           "2048->2x768, down 768->2048), top-8",
+                           "2048->2x768, down 768->2048), top-8", "roofline": moe_roof,
                "parallelism": f"ep{world}: experts sharded; one clefq_moe_ep_layer call, dispatch and return "
                               "stored into peers' buffers over NVLink by the kernels" if world > 1
                else "single GPU", "tokens_per_s": world * MOE_T / (mms / 1000), "ms_per_step": mms,
@@ -419,7 +426,15 @@ def run_clefq(args, world, rank, local):
         nms = timed(lambda: mlp_tp(tx, tshard))
         barrier(world)
         comm.close()
+        # fused compute+collective roofline: the slower of (int ops / int8 peak) and (bytes this
+        # rank must put on NVLink / the measured 770 GB/s per direction)
+        tp_ops = 2.0 * M * HIDDEN * INTER * 3 / world
+        tp_link = (world - 1) * (M * (INTER // world) // 2 + M * (HIDDEN // world) * 2 + M * 4)
+        tp_target = max(tp_ops / (i8_peak * 1e12), tp_link / 770e9) * 1e3
         tp = {"workload": "C2 dense INT4 SwiGLU MLP block, 4096 tokens shared by all ranks",
+              "roofline": {"target_ms": tp_target, "frac": tp_target / fms, "int_ops_per_rank": tp_ops,
+                           "nvlink_bytes_per_rank": tp_link, "peaks": f"{i8_peak:.0f} TOP/s int8 (2 x measured "
+                           "bf16), 770 GB/s NVLink per direction (measured peer copy)"},
               "parallelism": f"tp{world}: intermediate sharded; one clefq_tp_mlp call whose packing kernel and "
                              "down-GEMM epilogue store their shards into every rank's buffer over NVLink, with "
                              "device barriers", "scaling": "strong",
