@@ -77,6 +77,9 @@ _SYMBOLS = {
     "clefq_tp_mlp_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i"]),
     "clefq_tp_mlp": (ctypes.c_int, ["p", "p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "p", "l"]),
     "clefq_tp_mlp_output": (ctypes.c_void_p, ["p", "l", "l", "l"]),
+    "clefq_untile_bf16": (ctypes.c_int, ["p", "p", "l", "l", "p"]),
+    "clefq_load_weight_workspace_size": (ctypes.c_int64, ["l", "l", "i", "i"]),
+    "clefq_load_weight": (ctypes.c_int, ["p", "p", "l", "l", "i", "i", "p", "p", "p", "l"]),
     "clefq_moe_ep_layer_region_bytes": (ctypes.c_int64, ["l", "l", "i", "i", "l"]),
     "clefq_moe_ep_layer_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i", "i", "i", "l"]),
     "clefq_moe_ep_layer": (ctypes.c_int, ["p", "p", "p", "p", "i", "l", "l", "l", "i", "i", "l", "p", "p", "p", "p", "p",
@@ -195,16 +198,32 @@ class QuantizedWeight:
     bits: int
 
 
-def load_quantized_weight(w, bits=4) -> QuantizedWeight:
-    """src/quantized.rs:147-234 minus checkpoint untiling: BF16 [rows][cols] logical rows
-    -> prepare (weights rotate and quantize like activations) -> retile."""
+def load_quantized_weight(w, bits=4, tiled=False) -> QuantizedWeight:
+    """src/quantized.rs:147-234 (after the precision policy, which `clefq.loading` holds): BF16
+    [rows][cols] -> prepare (weights rotate and quantize like activations) -> retile, one
+    clefq_load_weight call.  tiled=True: w holds the checkpoint's tiled256x64 byte order
+    (src/checkpoint.rs:20-100) under its logical [rows][cols] shape."""
+    _need_cuda(w)
     rows, cols = w.shape
     if rows % 256 or cols % 256:
         raise ValueError("unsupported quantized weight shape")
-    stride = stride_for(cols, bits)
-    p = prepare(w, bits, stride, operand=False)
-    codes = retile_codes(p.codes, rows, cols, bits)
-    return QuantizedWeight(codes, p.scales.clone(), rows, cols, stride, bits)
+    w = w.contiguous()
+    codes = torch.empty(rows * cols * bits // 32, dtype=torch.int32, device=w.device)
+    scales = torch.empty(rows, dtype=torch.float32, device=w.device)
+    need = lib().clefq_load_weight_workspace_size(rows, cols, bits, int(tiled))
+    ws = torch.empty(need, dtype=torch.uint8, device=w.device)
+    _call("clefq_load_weight", _stream(), _ptr(w), rows, cols, bits, int(tiled), _ptr(codes), _ptr(scales), _ptr(ws),
+          need)
+    return QuantizedWeight(codes, scales, rows, cols, stride_for(cols, bits), bits)
+
+
+def untile_bf16(w):
+    """Checkpoint tiled256x64 order -> row-major rows (src/checkpoint.rs:67-100), on the device."""
+    _need_cuda(w)
+    rows, cols = w.shape
+    out = torch.empty_like(w)
+    _call("clefq_untile_bf16", _stream(), _ptr(w.contiguous()), rows, cols, _ptr(out))
+    return out
 
 
 # ---------------------------------------------------------------------------------------

@@ -90,6 +90,19 @@ CLEFQ_API int clefq_retile(void *stream, const void *codes, int64_t rows, int64_
                            void *out);
 
 /*
+ * Weight loading (src/quantized.rs:147-234 load_quantized_weight, after its precision policy):
+ * BF16 [rows][cols] -> prepare with stride cols (+512/bits when cols % 1024 == 0) -> retile.
+ * tiled != 0: src is in the checkpoint's tiled256x64 layout (src/checkpoint.rs:20-100,
+ * [rows/256][cols/64][256][64]) and is restored to rows on the device.  Outputs the tiled codes
+ * (rows*cols*bits/8 bytes) and the f32 scale row.  rows and cols must be multiples of 256
+ * (the reference's ensure!).
+ */
+CLEFQ_API int clefq_untile_bf16(void *stream, const void *src, int64_t rows, int64_t cols, void *dst);
+CLEFQ_API int64_t clefq_load_weight_workspace_size(int64_t rows, int64_t cols, int bits, int tiled);
+CLEFQ_API int clefq_load_weight(void *stream, const void *src, int64_t rows, int64_t cols, int bits, int tiled,
+                                void *codes_tiled, float *scales, void *workspace, int64_t workspace_bytes);
+
+/*
  * Dense quantized projection; replaces project_prepared + h3_gemm_i{4,8}_256[_residual]
  * (src/quantized.rs:470-537, kernels/gemm_integer.loom:394-433):
  *   y = (f32(sum_k a*w) * w_scales[n]) * a_scales[m] + 0
