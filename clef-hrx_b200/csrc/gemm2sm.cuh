@@ -386,23 +386,37 @@ __global__ void __launch_bounds__(THREADS2, 1)
             }
           }
         }
+        if (!GROUPED && p.out_f32) {
+          // F32 output: the reference's epilogue value, stored as it is computed
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float as = __shfl_sync(0xffffffffu, my_scale[q], j);
-          const float a = __int2float_rn((int)accv[j] >> shift);
-          uint16_t h;
-          if (GROUPED) {
-            h = f32_to_bf16(__fmul_rn(a, __fmul_rn(as, ws)));
-          } else {
+          for (int j = 0; j < 32; ++j) {
+            const float as = __shfl_sync(0xffffffffu, my_scale[q], j);
+            const float a = __int2float_rn((int)accv[j] >> shift);
             const float y = __fadd_rn(__fmul_rn(__fmul_rn(a, ws), as), 0.0f);
-            if (p.out_f32) {
-              if (c + j < rows_valid) p.out_f32[(row0 + c + j) * p.ldo + col0 + r] = y;
-              continue;
-            }
-            const float sat = maxnum(minnum(y, big), -big);
-            h = f32_to_bf16(fabsf(y) < __int_as_float(0x7f800000) ? sat : y);
+            if (c + j < rows_valid) p.out_f32[(row0 + c + j) * p.ldo + col0 + r] = y;
           }
-          staging[(c + j) * 128 + r] = h;
+          continue;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          float y[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const float as = __shfl_sync(0xffffffffu, my_scale[q], j + u);
+            const float a = __int2float_rn((int)accv[j + u] >> shift);
+            if (GROUPED) {
+              y[u] = __fmul_rn(a, __fmul_rn(as, ws));
+            } else {
+              // finite values saturate to the largest finite BF16; infinities and NaN pass
+              const float v = __fadd_rn(__fmul_rn(__fmul_rn(a, ws), as), 0.0f);
+              y[u] = fabsf(v) < __int_as_float(0x7f800000) ? maxnum(minnum(v, big), -big) : v;
+            }
+          }
+          // two tokens rounded to BF16 (nearest even) by one cvt.rn.bf16x2; a NaN stays a NaN
+          uint32_t h2;
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(y[1]), "f"(y[0]));
+          staging[(c + j) * 128 + r] = (uint16_t)h2;
+          staging[(c + j + 1) * 128 + r] = (uint16_t)(h2 >> 16);
         }
       }
       if (GROUPED || !p.out_f32) {
