@@ -415,7 +415,7 @@ static void launch_variant(dim3 grid, const CUtensorMap &t, const CUtensorMap &w
 }
 
 // Launch the pair kernel on as many co-resident clusters of 2 as the device holds.
-template <bool G, int B>
+template <bool G, int B, int SUB = 1>
 static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, const CUtensorMap &w0,
                                       const CUtensorMap &w1, const GemmParams &p, cudaStream_t stream) {
   using namespace two_sm;
@@ -424,7 +424,7 @@ static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, 
   cudaGetDevice(&dev);
   int scratch = 0;
   int &max_clusters = (dev >= 0 && dev < 64) ? max_clusters_dev[dev] : scratch;
-  auto kern = gemm_i8_2sm_kernel<G, B>;
+  auto kern = gemm_i8_2sm_kernel<G, B, SUB>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -432,12 +432,12 @@ static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, 
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(THREADS2);
-  cfg.dynamicSmemBytes = Cfg2<B>::SMEM;
+  cfg.dynamicSmemBytes = Cfg2<B, SUB>::SMEM;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (!max_clusters) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<B>::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<B, SUB>::SMEM);
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(2 * 74);
     int n = 0;
@@ -523,6 +523,13 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
     }
     const int64_t pair_tiles = tiles_m * (p.n / two_sm::BMP);
     cudaError_t e;
+    // dense int4 with at least two token tiles: two sub-tiles per pair tile sharing each
+    // converted weight stage
+    if (!p.grouped && p.bits == 4 && p.m >= 2 * two_sm::BN2) {
+      const int64_t pair_tiles2 = ((p.m + 2 * two_sm::BN2 - 1) / (2 * two_sm::BN2)) * (p.n / two_sm::BMP);
+      e = launch_variant_2sm<false, 4, 2>(pair_tiles2, tmap, wmap0, wmap1, p, stream);
+      return e == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+    }
     if (p.grouped)
       e = p.bits == 4 ? launch_variant_2sm<true, 4>(pair_tiles, tmap, wmap0, wmap1, p, stream)
                       : launch_variant_2sm<true, 8>(pair_tiles, tmap, wmap0, wmap1, p, stream);

@@ -40,13 +40,21 @@ constexpr int STAGING2 = BN2 * 128 * 2;        // 48 KiB BF16 [token][column]
 // them complete, so their ring must cover the TMA latency (~3k cycles under load) plus a
 // stage: 5 slots.  Weight slots are copied into registers by the converters as soon as
 // they land (before waiting for a free TMEM stage), so 3 slots keep them ahead.
-template <int BITS>
+//
+// SUB = 2 (dense int4 only): a pair tile spans two 192-token sub-tiles that share every
+// converted weight stage -- per K step the leader issues one MMA into each sub-tile's
+// accumulator, twice the tensor work per pass of the converter -> MMA -> commit chain.  The
+// two accumulators then fill the TMEM columns that SUB = 1 uses for double buffering, so the
+// epilogue of a tile no longer overlaps the next tile's mainloop; token stages hold both
+// sub-tiles (48 KiB), 3 of them, and 2 weight slots, to fit shared memory.
+template <int BITS, int SUB = 1>
 struct Cfg2 {
-  static constexpr int NT = BITS == 4 ? 5 : 4;            // token stages (24 KiB each)
-  static constexpr int NW = BITS == 4 ? 3 : 2;            // weight stages
+  static constexpr int TOK_STAGE = SUB * TOK_B;           // token bytes per stage and CTA
+  static constexpr int NT = SUB == 2 ? 3 : (BITS == 4 ? 5 : 4);   // token stages
+  static constexpr int NW = SUB == 2 ? 2 : (BITS == 4 ? 3 : 2);   // weight stages
   static constexpr int W_BYTES = 128 * KS2 * BITS / 8;
-  static constexpr int W_OFF = NT * TOK_B;                // weight ring after the token ring
-  static constexpr int RING = NT * TOK_B + NW * W_BYTES;
+  static constexpr int W_OFF = NT * TOK_STAGE;            // weight ring after the token ring
+  static constexpr int RING = NT * TOK_STAGE + NW * W_BYTES;
   static constexpr int SMEM = RING + STAGING2 + 1024 + 1024;
 };
 
@@ -61,6 +69,7 @@ struct Smem2 {
 
 struct TileMap2 {
   int n_pairs, total;
+  int span;  // token rows per pair tile (dense): SUB x BN2
   CQ_DEV bool get(const GemmParams &p, int t, int64_t &row0, int &rows_valid, int &np, int &expert) const {
     if (t >= total) return false;
     const int mt = t / n_pairs;
@@ -72,8 +81,8 @@ struct TileMap2 {
       rows_valid = (int)(end - row0 < BN2 ? end - row0 : BN2);
     } else {
       expert = 0;
-      row0 = (int64_t)mt * BN2;
-      rows_valid = (int)(p.m - row0 < BN2 ? p.m - row0 : BN2);
+      row0 = (int64_t)mt * span;
+      rows_valid = (int)(p.m - row0 < span ? p.m - row0 : span);
     }
     return true;
   }
@@ -125,11 +134,12 @@ CQ_DEV void store_tile_rows(const GemmParams &p, const uint16_t *staging, int64_
   }
 }
 
-template <bool GROUPED, int BITS>
+template <bool GROUPED, int BITS, int SUB = 1>
 __global__ void __launch_bounds__(THREADS2, 1)
     gemm_i8_2sm_kernel(const __grid_constant__ CUtensorMap tok_map, const __grid_constant__ CUtensorMap w_map0,
                        const __grid_constant__ CUtensorMap w_map1, GemmParams p) {
-  using C = Cfg2<BITS>;
+  static_assert(SUB == 1 || (SUB == 2 && !GROUPED && BITS == 4), "two sub-tiles: dense int4 only");
+  using C = Cfg2<BITS, SUB>;
   constexpr int NT = C::NT, NW = C::NW;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -142,7 +152,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
 
   TileMap2 tm;
   tm.n_pairs = p.n / BMP;
-  tm.total = (GROUPED ? p.tile_list[0] : (int)((p.m + BN2 - 1) / BN2)) * tm.n_pairs;
+  tm.span = SUB * BN2;
+  tm.total = (GROUPED ? p.tile_list[0] : (int)((p.m + tm.span - 1) / tm.span)) * tm.n_pairs;
   if (cluster >= tm.total) return;  // uniform across the pair
   const int k_stages = p.k / KS2;
   const int blocks_k = p.k / (32 * (32 / BITS));
@@ -211,9 +222,12 @@ __global__ void __launch_bounds__(THREADS2, 1)
                       w_row_tile * blocks_k + kb * (BITS == 4 ? 1 : 2));
           // token box: x = 128 bytes of a K slice, y = 96 rows, z = the stage's two K slices
           if (!(ok = mbar_wait_bounded(&s.tok_empty[st], ((g / NT) & 1) ^ 1, &s.err, 1))) break;
-          if (rank == 0) mbar_arrive_expect_tx(&s.tok_full[st], 2 * TOK_B);
-          tma_load_3d_cg2(ring + st * TOK_B, &tok_map, mapa_shared(smem_u32(&s.tok_full[st]), 0), 0,
-                          (int)(row0 + HALF * rank), 2 * kb);
+          if (rank == 0) mbar_arrive_expect_tx(&s.tok_full[st], SUB * 2 * TOK_B);
+#pragma unroll
+          for (int sb = 0; sb < SUB; ++sb)
+            tma_load_3d_cg2(ring + st * C::TOK_STAGE + sb * TOK_B, &tok_map,
+                            mapa_shared(smem_u32(&s.tok_full[st]), 0), 0, (int)(row0 + sb * BN2 + HALF * rank),
+                            2 * kb);
         }
       }
     }
@@ -226,8 +240,11 @@ __global__ void __launch_bounds__(THREADS2, 1)
       int64_t row0;
       int rows_valid, np, expert;
       for (int t = cluster; ok && tm.get(p, t, row0, rows_valid, np, expert); t += nclusters, ++i) {
-        const int buf = i & 1;
-        if (!(ok = mbar_wait_bounded(&s.acc_empty[buf], ((i >> 1) & 1) ^ 1, &s.err, 7))) break;
+        // SUB = 1: accumulator buffer i & 1 (double buffered); SUB = 2: both buffers, one
+        // per sub-tile, released together by the epilogue
+        const int buf = SUB == 1 ? (i & 1) : 0;
+        const uint32_t par = SUB == 1 ? (((i >> 1) & 1) ^ 1) : ((i & 1) ^ 1);
+        if (!(ok = mbar_wait_bounded(&s.acc_empty[buf], par, &s.err, 7))) break;
         tc_fence_after();
         const uint32_t acc = tmem + ACC_COLS * buf;
         for (int kb = 0; kb < k_stages; ++kb, ++g) {
@@ -237,16 +254,25 @@ __global__ void __launch_bounds__(THREADS2, 1)
                      mbar_wait_bounded(&s.wtm_full[sw], (g / NSW) & 1, &s.err, 3)))
             break;
           tc_fence_after();
-          const uint32_t b_base = smem_u32(ring + st * TOK_B);
+          const uint32_t b_base = smem_u32(ring + st * C::TOK_STAGE);
 #pragma unroll
-          for (int j = 0; j < KS2 / 32; ++j)
-            mma_i8_ts2(acc, tmem + WCOL + 64 * sw + 8 * j, smem_desc_sw128(b_base + (j >> 2) * (TOK_B / 2) + 32 * (j & 3)),
-                       IDESC2, (kb | j) != 0);
+          for (int j = 0; j < KS2 / 32; ++j) {
+            const uint32_t a_col = tmem + WCOL + 64 * sw + 8 * j;
+            const uint32_t b_off = (j >> 2) * (TOK_B / 2) + 32 * (j & 3);
+#pragma unroll
+            for (int sb = 0; sb < SUB; ++sb)
+              mma_i8_ts2(acc + ACC_COLS * sb, a_col, smem_desc_sw128(b_base + sb * TOK_B + b_off), IDESC2,
+                         (kb | j) != 0);
+          }
           mma_commit2_mc(&s.tok_empty[st], 3);
         }
         mma_commit2_mc(&s.acc_full[buf], 3);
       }
-      if (i > 0) mbar_wait_bounded(&s.acc_full[(i - 1) & 1], ((i - 1) >> 1) & 1, &s.err, 6);
+      if (i > 0) {
+        const int last = SUB == 1 ? ((i - 1) & 1) : 0;
+        const uint32_t par = SUB == 1 ? (((i - 1) >> 1) & 1) : ((i - 1) & 1);
+        mbar_wait_bounded(&s.acc_full[last], par, &s.err, 6);
+      }
     }
   } else if (warp < 4) {
     // ---- weight converters (both CTAs) -> own TMEM; stage-ready counted on the leader ----
@@ -343,19 +369,22 @@ __global__ void __launch_bounds__(THREADS2, 1)
     int64_t row0;
     int rows_valid, np, expert;
     for (int t = cluster; tm.get(p, t, row0, rows_valid, np, expert); t += nclusters, ++i) {
-      const int buf = i & 1;
-      float my_scale[CH];
+      // SUB = 1: this tile's accumulator is buffer i & 1; SUB = 2: sub-tile sb is buffer sb
+      float my_scale[SUB][CH];
 #pragma unroll
-      for (int q = 0; q < CH; ++q) {
-        const int mj = ehalf * (BN2 / 2) + 32 * q + lane;
-        my_scale[q] = 0.0f;
-        if (mj < rows_valid) {
-          const int64_t pos = row0 + mj;
-          if (GROUPED) {
-            const int64_t route = p.perm[pos];
-            my_scale[q] = p.a_scales[p.scale_mode == 0 ? pos : (p.scale_mode == 1 ? route / p.topk : route)];
-          } else {
-            my_scale[q] = p.a_scales[pos];
+      for (int sb = 0; sb < SUB; ++sb) {
+#pragma unroll
+        for (int q = 0; q < CH; ++q) {
+          const int mj = sb * BN2 + ehalf * (BN2 / 2) + 32 * q + lane;
+          my_scale[sb][q] = 0.0f;
+          if (mj < rows_valid) {
+            const int64_t pos = row0 + mj;
+            if (GROUPED) {
+              const int64_t route = p.perm[pos];
+              my_scale[sb][q] = p.a_scales[p.scale_mode == 0 ? pos : (p.scale_mode == 1 ? route / p.topk : route)];
+            } else {
+              my_scale[sb][q] = p.a_scales[pos];
+            }
           }
         }
       }
@@ -363,69 +392,78 @@ __global__ void __launch_bounds__(THREADS2, 1)
       weight_tile(np, expert, which, w_row_tile);
       const float ws = p.w_scales[which][(int64_t)w_row_tile * 128 + r];
       const int col0 = (2 * np + (int)rank) * 128;  // first output column of this CTA
+      const int done_buf = SUB == 1 ? (i & 1) : 0;  // the barrier pair of this tile
       bool have = true;
-      if (lane == 0) have = mbar_wait_bounded(&s.acc_full[buf], (i >> 1) & 1, &s.err, 5);
+      if (lane == 0)
+        have = mbar_wait_bounded(&s.acc_full[done_buf], SUB == 1 ? ((i >> 1) & 1) : (i & 1), &s.err, 5);
       have = __shfl_sync(0xffffffffu, have, 0) != 0;
       if (!named_barrier_and(2, 32 * EPI_WARPS, have)) break;
       tc_fence_after();
 #pragma unroll
-      for (int q = 0; q < CH; ++q) {
-        const int c = ehalf * (BN2 / 2) + 32 * q;
-        uint32_t accv[32];
-        tmem_ld_x32(tmem + lane_base + ACC_COLS * buf + c, accv);
-        tmem_ld_wait();
-        if (q == CH - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if (rank == 0) {
-              if (eidx == 0) mbar_arrive_expect_tx(&s.acc_empty[buf], 4 * EPI_WARPS);
-              else mbar_arrive(&s.acc_empty[buf]);
-            } else {
-              st_async_signal(lead_sink, lead_acc_empty + 8 * buf);
+      for (int sb = 0; sb < SUB; ++sb) {
+        const int buf = SUB == 1 ? (i & 1) : sb;
+        const int64_t srow0 = row0 + sb * BN2;
+        const int svalid = rows_valid - sb * BN2;  // may be <= 0: nothing of the sub-tile is stored
+#pragma unroll
+        for (int q = 0; q < CH; ++q) {
+          const int c = ehalf * (BN2 / 2) + 32 * q;
+          uint32_t accv[32];
+          tmem_ld_x32(tmem + lane_base + ACC_COLS * buf + c, accv);
+          tmem_ld_wait();
+          if (q == CH - 1 && sb == SUB - 1) {
+            // every accumulator column of the tile is in registers: release the buffer(s)
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if (rank == 0) {
+                if (eidx == 0) mbar_arrive_expect_tx(&s.acc_empty[done_buf], 4 * EPI_WARPS);
+                else mbar_arrive(&s.acc_empty[done_buf]);
+              } else {
+                st_async_signal(lead_sink, lead_acc_empty + 8 * done_buf);
+              }
             }
           }
-        }
-        if (!GROUPED && p.out_f32) {
-          // F32 output: the reference's epilogue value, stored as it is computed
+          if (!GROUPED && p.out_f32) {
+            // F32 output: the reference's epilogue value, stored as it is computed
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float as = __shfl_sync(0xffffffffu, my_scale[q], j);
-            const float a = __int2float_rn((int)accv[j] >> shift);
-            const float y = __fadd_rn(__fmul_rn(__fmul_rn(a, ws), as), 0.0f);
-            if (c + j < rows_valid) p.out_f32[(row0 + c + j) * p.ldo + col0 + r] = y;
-          }
-          continue;
-        }
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          float y[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float as = __shfl_sync(0xffffffffu, my_scale[q], j + u);
-            const float a = __int2float_rn((int)accv[j + u] >> shift);
-            if (GROUPED) {
-              y[u] = __fmul_rn(a, __fmul_rn(as, ws));
-            } else {
-              // finite values saturate to the largest finite BF16; infinities and NaN pass
-              const float v = __fadd_rn(__fmul_rn(__fmul_rn(a, ws), as), 0.0f);
-              y[u] = fabsf(v) < __int_as_float(0x7f800000) ? maxnum(minnum(v, big), -big) : v;
+            for (int j = 0; j < 32; ++j) {
+              const float as = __shfl_sync(0xffffffffu, my_scale[sb][q], j);
+              const float a = __int2float_rn((int)accv[j] >> shift);
+              const float y = __fadd_rn(__fmul_rn(__fmul_rn(a, ws), as), 0.0f);
+              if (c + j < svalid) p.out_f32[(srow0 + c + j) * p.ldo + col0 + r] = y;
             }
+            continue;
           }
-          // two tokens rounded to BF16 (nearest even) by one cvt.rn.bf16x2; a NaN stays a NaN
-          uint32_t h2;
-          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(y[1]), "f"(y[0]));
-          staging[(c + j) * 128 + r] = (uint16_t)h2;
-          staging[(c + j + 1) * 128 + r] = (uint16_t)(h2 >> 16);
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float y[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float as = __shfl_sync(0xffffffffu, my_scale[sb][q], j + u);
+              const float a = __int2float_rn((int)accv[j + u] >> shift);
+              if (GROUPED) {
+                y[u] = __fmul_rn(a, __fmul_rn(as, ws));
+              } else {
+                // finite values saturate to the largest finite BF16; infinities and NaN pass
+                const float v = __fadd_rn(__fmul_rn(__fmul_rn(a, ws), as), 0.0f);
+                y[u] = fabsf(v) < __int_as_float(0x7f800000) ? maxnum(minnum(v, big), -big) : v;
+              }
+            }
+            // two tokens rounded to BF16 (nearest even) by one cvt.rn.bf16x2; a NaN stays a NaN
+            uint32_t h2;
+            asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(y[1]), "f"(y[0]));
+            staging[(c + j) * 128 + r] = (uint16_t)h2;
+            staging[(c + j + 1) * 128 + r] = (uint16_t)(h2 >> 16);
+          }
         }
-      }
-      if (GROUPED || !p.out_f32) {
-        named_barrier_sync(1, 32 * EPI_WARPS);
-        // each warp stores 24 token rows, 256 contiguous bytes per row
-        const int m0 = eidx * (BN2 / EPI_WARPS);
-        if (p.store16) store_tile_rows<GROUPED, 8>(p, staging, row0, rows_valid, col0, m0, m0 + BN2 / EPI_WARPS, lane);
-        else store_tile_rows<GROUPED, 4>(p, staging, row0, rows_valid, col0, m0, m0 + BN2 / EPI_WARPS, lane);
-        named_barrier_sync(1, 32 * EPI_WARPS);
+        if (GROUPED || !p.out_f32) {
+          named_barrier_sync(1, 32 * EPI_WARPS);
+          // each warp stores 24 token rows, 256 contiguous bytes per row
+          const int m0 = eidx * (BN2 / EPI_WARPS);
+          if (p.store16) store_tile_rows<GROUPED, 8>(p, staging, srow0, svalid, col0, m0, m0 + BN2 / EPI_WARPS, lane);
+          else store_tile_rows<GROUPED, 4>(p, staging, srow0, svalid, col0, m0, m0 + BN2 / EPI_WARPS, lane);
+          named_barrier_sync(1, 32 * EPI_WARPS);
+        }
       }
     }
   }
