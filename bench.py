@@ -11,6 +11,10 @@ write between timed steps; each step is timed with CUDA events on the launching 
 
 Multi-GPU: one process per GPU (torchrun); every rank runs its own 4096-token block with
 replicated weights (data-parallel replicas, no collective on the data path): weak scaling.
+The `secondary` line runs the C4 MoE layer expert-parallel (clefq_moe_ep_layer, dispatch and
+return stored into peers' buffers by the kernels; the NCCL all-to-all composition timed
+beside it) and the `tensor_parallel` line one C2 block split over the ranks (clefq_tp_mlp).
+`e2e` streams host rows through clefq.mlp_host, copies included.
 --impl reference: the reference's CPU semantics (the C/OpenMP oracle port; the reference
 itself is Rust + hrx-rs on an AMD gfx1151 and cannot run here) on the host cores, rank 0.
 """
