@@ -110,7 +110,8 @@ static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_
                        int64_t aux_ld, int64_t rows, int64_t width, int64_t stride, void *out, void *operand,
                        int64_t operand_ld, void *norm_out, int64_t norm_ld, float *rowmax_out = nullptr,
                        const float *rowmax_in = nullptr, uint32_t *const *code_dst = nullptr,
-                       int n_code_dst = 0, int64_t code_ld = 0, const int64_t *rows_dev = nullptr) {
+                       int n_code_dst = 0, int64_t code_ld = 0, const int64_t *rows_dev = nullptr,
+                       const int *dup_rows = nullptr, int dup = 0) {
   int rc = check_prepare(kind, bits, rows, width, stride);
   if (rc) return rc;
   if (!x || (!out && !rowmax_out) || (kind != CLEFQ_PREP_PLAIN && !aux) ||
@@ -152,6 +153,8 @@ static int run_prepare(cudaStream_t s, int kind, int bits, const void *x, int64_
   a.n_code_dst = n_code_dst;
   a.code_ld = code_ld;
   a.rows_dev = rows_dev;
+  a.dup_rows = dup_rows;
+  a.dup = dup;
   return launch_prepare(a, s);  // sets clefq_last_error() itself on failure
 }
 
@@ -706,7 +709,7 @@ static int run_expert_ffn(cudaStream_t s, const uint8_t *xs, int64_t nroutes, co
 // ---- fused Omni MoE block --------------------------------------------------------------
 struct MoeTables {
   float *routes, *order;
-  int *counts, *offsets, *tiles, *perm;
+  int *counts, *offsets, *tiles, *perm, *slots;
   uint32_t *xq, *hq;
   uint8_t *x8, *xs, *h8;
   uint16_t *gu, *values;
@@ -719,6 +722,7 @@ static Arena moe_tables(Arena a, int64_t tokens, int64_t hidden, int64_t inter, 
   t.offsets = a.take<int>(experts + 1);
   t.tiles = a.take<int>(1 + 2 * ((routes + 127) / 128 + experts));
   t.perm = a.take<int>(routes);
+  t.slots = a.take<int>(routes);
   t.xq = a.take<uint32_t>(tokens * (stride_for(hidden) / 8 + 1));
   t.x8 = a.take<uint8_t>(tokens * hidden);
   t.xs = a.take<uint8_t>(routes * hidden);
@@ -757,15 +761,42 @@ int clefq_moe(void *stream, const void *x, const void *logits, int logits_dtype,
     return set_err(CLEFQ_ERR_SHAPE, "hidden and intermediate must both be multiples of 256, or neither");
   }
   int rc = launch_route(logits, logits_dtype == CLEFQ_F32, tokens, experts, topk, routes, s);
-  if (!rc)
-    rc = launch_group(routes, tokens, topk, experts, tile_rows, t.counts, t.offsets, t.tiles, t.perm, nullptr, t.order,
-                      nullptr, s, sms);
   if (rc) return cuda_err("routing launch");
+  // the stable grouping also gives every route its expert-sorted row (slots; -1 for a route
+  // left out), so packing x can write each token's operand straight to its routes' rows
+  if (cudaMemsetAsync(t.slots, 0xff, sizeof(int) * nroutes, s) != cudaSuccess) return cuda_err("slot reset");
+  {
+    SortArgs g{};
+    g.routes = routes;
+    g.route_ld = 2 * topk;
+    g.tokens = tokens;
+    g.topk = topk;
+    g.items = nroutes;
+    g.key_div = 1;
+    g.keys = experts;
+    g.dedupe = true;
+    g.hist = t.counts + experts;
+    g.counts = t.counts;
+    g.offsets = t.offsets;
+    g.tile_list = t.tiles;
+    g.tile_rows = tile_rows;
+    g.perm = t.perm;
+    g.slots = t.slots;
+    g.order = t.order;
+    if (launch_sort(g, s)) return cuda_err("routing launch");
+  }
   const int64_t sh = stride_for(hidden);
-  rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, tokens, hidden, sh, t.xq, t.x8, hidden, nullptr, 0);
-  if (rc) return rc;
-  rc = launch_gather(t.x8, hidden, t.perm, topk, nroutes, hidden, t.xs, hidden, s, sms);
-  if (rc) return cuda_err("gather launch");
+  if (topk <= kMaxDup && hidden <= 16384) {
+    rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, tokens, hidden, sh, t.xq, t.xs, hidden, nullptr, 0,
+                     nullptr, nullptr, nullptr, 0, 0, nullptr, t.slots, topk);
+    if (rc) return rc;
+  } else {
+    rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, tokens, hidden, sh, t.xq, t.x8, hidden, nullptr,
+                     0);
+    if (rc) return rc;
+    rc = launch_gather(t.x8, hidden, t.perm, topk, nroutes, hidden, t.xs, hidden, s, sms);
+    if (rc) return cuda_err("gather launch");
+  }
   rc = run_expert_ffn(s, t.xs, nroutes, reinterpret_cast<const float *>(t.xq + tokens * (sh / 8)), topk, t.tiles,
                       t.offsets, t.perm, experts, tile_rows, hidden, inter, gate_tiled, gate_scales, up_tiled,
                       up_scales, down_tiled, down_scales, t.gu, t.hq, t.h8, t.values);

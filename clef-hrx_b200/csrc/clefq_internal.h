@@ -9,6 +9,7 @@ namespace cq {
 
 constexpr int kMaxRanks = 8;              // ranks of a tensor-parallel group (one node)
 constexpr int kMaxPeers = kMaxRanks - 1;  // extra store destinations of a fused collective
+constexpr int kMaxDup = 8;                // operand rows one packed row can be written to
 
 struct PrepareArgs {
   const uint16_t *x;
@@ -38,6 +39,10 @@ struct PrepareArgs {
   // GEMM-input packing only: when set, only the first *rows_dev rows (<= rows) are packed;
   // the storage layout still spans `rows`
   const int64_t *rows_dev;
+  // plain int4 GEMM-input packing only: the s8 operand of input row r is stored at operand
+  // rows dup_rows[r * dup + d] (d < dup <= kMaxDup; negative entries skipped) instead of row r
+  const int *dup_rows;
+  int dup;
 };
 int launch_prepare(const PrepareArgs &a, cudaStream_t stream);
 int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);

@@ -590,6 +590,12 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
     const float inv = __fdiv_rn(0.0625f, scale);
     const bool finite = scale < __int_as_float(0x7f800000);
     uint32_t *orow = p.out + row * words;
+    constexpr bool DUP = !TAB && NS == 1;  // instance that can write the operand to several rows
+    int drow[kMaxDup];
+    if (DUP && p.dup) {
+#pragma unroll
+      for (int d = 0; d < kMaxDup; ++d) drow[d] = d < p.dup ? p.dup_rows[row * p.dup + d] : -1;
+    }
 #pragma unroll
     for (int sl = 0; sl < NS; ++sl) {
       const int g = gidx[sl];
@@ -614,9 +620,22 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
             if (d < p.n_code_dst) p.code_dst[d][cw] = w;
         }
         if (p.op8) {
-          uint8_t *op = p.op8 + row * p.op_ld + g * 256 + k * 64 + (r >> 2) * 32 + (r & 3) * 4;
-          *reinterpret_cast<uint32_t *>(op) = nib_lo16(w);
-          *reinterpret_cast<uint32_t *>(op + 16) = nib_hi16(w);
+          const int off = g * 256 + k * 64 + (r >> 2) * 32 + (r & 3) * 4;
+          const uint32_t lo = nib_lo16(w), hi = nib_hi16(w);
+          if (DUP && p.dup) {
+            // the row's operand goes to each of its routes' expert-sorted rows
+#pragma unroll
+            for (int d = 0; d < kMaxDup; ++d) {
+              if (drow[d] < 0) continue;
+              uint8_t *op = p.op8 + (int64_t)drow[d] * p.op_ld + off;
+              *reinterpret_cast<uint32_t *>(op) = lo;
+              *reinterpret_cast<uint32_t *>(op + 16) = hi;
+            }
+          } else {
+            uint8_t *op = p.op8 + row * p.op_ld + off;
+            *reinterpret_cast<uint32_t *>(op) = lo;
+            *reinterpret_cast<uint32_t *>(op + 16) = hi;
+          }
         }
       }
     }
@@ -712,7 +731,7 @@ bool try_launch_pack(PrepareArgs a, bool tab, cudaStream_t stream) {
   const int ngroups = a.width >> 8;
   const int sg = (ngroups + 3) / 4;  // slots of four groups
   const int ns = (sg + 15) / 16;
-  if (ns > (tab ? 1 : 2)) return false;
+  if (ns > (tab ? 1 : 2) || (a.dup && (tab || ns != 1))) return false;
   const int tw = (sg + ns - 1) / ns;
   const int rpb = 16 / tw > 0 ? 16 / tw : 1;
   const int threads = tw * 32 * rpb;
@@ -754,11 +773,13 @@ int launch_prepare(const PrepareArgs &a0, cudaStream_t stream) {
     return report_error(CLEFQ_ERR_SHAPE, "prepare: extra code destinations are for SwiGLU GEMM-input packing");
   if (a.rows_dev && !(gemm_input && (a.mode == MODE_PLAIN || tab)))
     return report_error(CLEFQ_ERR_SHAPE, "prepare: a device row count needs the GEMM-input kernel");
+  if (a.dup && (a.dup > kMaxDup || !a.dup_rows || !a.op8 || !gemm_input || a.mode != MODE_PLAIN))
+    return report_error(CLEFQ_ERR_SHAPE, "prepare: operand rows per input row need plain int4 GEMM-input packing");
   if (gemm_input && (a.mode == MODE_PLAIN || tab) && try_launch_pack(a, tab, stream)) {
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : report_error(CLEFQ_ERR_CUDA, cudaGetErrorString(e));
   }
-  if (a.n_code_dst || a.rows_dev)
+  if (a.n_code_dst || a.rows_dev || a.dup)
     return report_error(CLEFQ_ERR_SHAPE, "prepare: this launch shape needs the GEMM-input kernel");
   int tw, ch;
   if (norm) {
