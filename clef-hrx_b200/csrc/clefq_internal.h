@@ -43,6 +43,7 @@ struct PrepareArgs {
   // rows dup_rows[r * dup + d] (d < dup <= kMaxDup; negative entries skipped) instead of row r
   const int *dup_rows;
   int dup;
+  int narrow;           // set by the launcher: GEMM-input rows of 1..3 groups, one team per group
 };
 int launch_prepare(const PrepareArgs &a, cudaStream_t stream);
 int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);

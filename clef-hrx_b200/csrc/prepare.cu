@@ -462,7 +462,7 @@ CQ_DEV void cp_async_wait_dyn(int n) {
   else cp_async_wait<3>();
 }
 
-constexpr int kPackRedBytes = 4 * 16 * 4;  // [2][16] warp maxima, padded
+constexpr int kPackRedBytes = 2 * 64 * 4;  // [2][64] team maxima (16 warps x 4 teams)
 
 // NS slots (of four groups) per warp, team_warps warps per row, rows_per_block rows per
 // CTA; p.stages cp.async stages per thread of NS x NOP x 64 bytes each.
@@ -481,6 +481,16 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
   const int words = p.stride >> 3;
   const int code_words = p.width >> 3;
   const int q = lane >> 3, r = lane & 7;
+  // Narrow rows (G = 1..3 groups, NS = 1): each 8-lane team packs one group of one row, so a
+  // 16-warp block holds rpb = 64 / G rows and no team idles; the row maximum goes through
+  // shared memory.  Otherwise tw warps share a row and each team packs groups 4 apart.
+  const int G = NS == 1 ? p.narrow : 0;
+  const int Gd = G ? G : 1;      // divisor that is never zero
+  const int tau = warp * 4 + q;  // team of the block
+  const int tgroup = tau % Gd;   // narrow: this team's group of its row
+  const int team_row = G ? tau / Gd : team;
+  const bool team_on = G ? tau < rpb * G : true;
+  const bool row_leader = G ? (team_on && tgroup == 0 && r == 0) : tid_team == 0;
   // rows to pack: p.rows, or fewer when the count is only known on the device (the code
   // and scale layout always spans p.rows)
   int64_t nrows = p.rows;
@@ -494,10 +504,10 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
   const uint32_t stage_bytes = (uint32_t)(NS * NOP * 4) * chunk;
   int gidx[NS];                                              // this lane's group per slot
 #pragma unroll
-  for (int sl = 0; sl < NS; ++sl) gidx[sl] = (sl * tw + wt) * 4 + q;
+  for (int sl = 0; sl < NS; ++sl) gidx[sl] = G ? (team_on ? tgroup : ngroups) : (sl * tw + wt) * 4 + q;
 
   auto issue = [&](int64_t b, int stg) {
-    const int64_t row = b * rpb + team;
+    const int64_t row = b * rpb + team_row;
     const bool ok = b < nblk && row < nrows;
     const uint32_t base = stage0 + stg * stage_bytes + threadIdx.x * 16;
 #pragma unroll
@@ -527,8 +537,8 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
   }
   int par = 0, st = 0;
   for (; blk < nblk; blk += gridDim.x, par ^= 1) {
-    const int64_t row = blk * rpb + team;
-    const bool row_ok = row < nrows;
+    const int64_t row = blk * rpb + team_row;
+    const bool row_ok = team_on && row < nrows;
     cp_async_wait_dyn(nstg - 1);  // this block's copies (all but the nstg-1 newest groups)
     const uint32_t base = stage0 + st * stage_bytes + threadIdx.x * 16;
     float v[NS][32];
@@ -569,19 +579,34 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
 #pragma unroll
       for (int i = 0; i < 32; i += 2) m = absmax3_nan(m, v[sl][i], v[sl][i + 1]);
     }
+    float rmax = 0.0f;
+    if (G) {
+      // the team's group maximum, then the maximum over the row's G teams
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if (m != m) m = __int_as_float(0x7f800000);
-    float *rs = red + par * slots + team * tw;
-    if (lane == 0) rs[wt] = m;
-    __syncthreads();
-    float rmax = lane < tw ? rs[lane] : 0.0f;
+      for (int off = 4; off >= 1; off >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, off));
+      if (m != m) m = __int_as_float(0x7f800000);
+      float *rs = red + par * 64;
+      if (r == 0) rs[tau] = m;
+      __syncthreads();
+      if (team_on) {
+        const int first = tau - tgroup;
+        for (int j = 0; j < G; ++j) rmax = maxnum(rmax, rs[first + j]);
+      }
+    } else {
 #pragma unroll
-    for (int off = 8; off >= 1; off >>= 1) rmax = maxnum(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
-    rmax = __shfl_sync(0xffffffffu, rmax, 0);
+      for (int off = 16; off >= 1; off >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, off));
+      if (m != m) m = __int_as_float(0x7f800000);
+      float *rs = red + par * slots + team * tw;
+      if (lane == 0) rs[wt] = m;
+      __syncthreads();
+      rmax = lane < tw ? rs[lane] : 0.0f;
+#pragma unroll
+      for (int off = 8; off >= 1; off >>= 1) rmax = maxnum(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+      rmax = __shfl_sync(0xffffffffu, rmax, 0);
+    }
     if (!row_ok) continue;
     if (p.rowmax_out) {
-      if (tid_team == 0) p.rowmax_out[row] = rmax;
+      if (row_leader) p.rowmax_out[row] = rmax;
       continue;
     }
     if (p.rowmax_in) rmax = p.rowmax_in[row];
@@ -640,8 +665,12 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
       }
     }
     // Stride padding words are zeroed; the scale follows all code rows.
-    for (int w = code_words + tid_team; w < words; w += tw * 32) orow[w] = 0u;
-    if (tid_team == 0) reinterpret_cast<float *>(p.out + p.rows * words)[row] = scale;
+    if (!G) {
+      for (int w = code_words + tid_team; w < words; w += tw * 32) orow[w] = 0u;
+    } else if (tgroup == 0) {
+      for (int w = code_words + r; w < words; w += 8) orow[w] = 0u;
+    }
+    if (row_leader) reinterpret_cast<float *>(p.out + p.rows * words)[row] = scale;
   }
   cp_async_wait<0>();
 }
@@ -733,8 +762,12 @@ bool try_launch_pack(PrepareArgs a, bool tab, cudaStream_t stream) {
   const int ns = (sg + 15) / 16;
   if (ns > (tab ? 1 : 2) || (a.dup && (tab || ns != 1))) return false;
   const int tw = (sg + ns - 1) / ns;
-  const int rpb = 16 / tw > 0 ? 16 / tw : 1;
-  const int threads = tw * 32 * rpb;
+  // rows of fewer than four groups: one group per 8-lane team (narrow mode), 64 / G rows per
+  // 16-warp block; wider rows: tw warps per row
+  const bool narrow = ngroups < 4 && ns == 1;
+  const int rpb = narrow ? 64 / ngroups : (16 / tw > 0 ? 16 / tw : 1);
+  const int threads = narrow ? 512 : tw * 32 * rpb;
+  a.narrow = narrow ? ngroups : 0;
   const size_t per_stage = (size_t)threads * ns * (tab ? 2 : 1) * 64;
   int stages = (int)(((tab ? 96 : 128) * 1024) / per_stage);
   if (stages > 4) stages = 4;
