@@ -23,6 +23,8 @@
 // No TMA multicast anywhere (safe in multi-GPU builds).
 #include <cuda.h>
 
+#include <atomic>
+
 #include "clefq_internal.h"
 #include "cq_common.cuh"
 
@@ -361,14 +363,15 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
+  // a function-local static is initialised once, even with concurrent first callers
+  static const EncodeTiledFn fn = [] {
     void *ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
+      return reinterpret_cast<EncodeTiledFn>(ptr);
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
   return fn;
 }
 
@@ -404,12 +407,12 @@ static bool weight_map_blocks(EncodeTiledFn enc, CUtensorMap *m, const uint32_t 
 template <bool G, int B>
 static void launch_variant(dim3 grid, const CUtensorMap &t, const CUtensorMap &w0, const CUtensorMap &w1,
                            const GemmParams &p, cudaStream_t stream) {
-  static bool attr[64];  // per device: the shared-memory limit is a per-context attribute
+  static std::atomic<bool> attr[64];  // per device: the shared-memory limit is a per-context attribute
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr[dev]) {
+  if (dev < 0 || dev >= 64 || !attr[dev].load(std::memory_order_acquire)) {
     cudaFuncSetAttribute(gemm_i8_kernel<G, B>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<B>::SMEM);
-    if (dev >= 0 && dev < 64) attr[dev] = true;
+    if (dev >= 0 && dev < 64) attr[dev].store(true, std::memory_order_release);
   }
   gemm_i8_kernel<G, B><<<grid, THREADS, Cfg<B>::SMEM, stream>>>(t, w0, w1, p);
 }
@@ -419,11 +422,13 @@ template <bool G, int B, int SUB = 1>
 static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, const CUtensorMap &w0,
                                       const CUtensorMap &w1, const GemmParams &p, cudaStream_t stream) {
   using namespace two_sm;
-  static int max_clusters_dev[64];  // per device, like the shared-memory attribute
+  // per device, like the shared-memory attribute; set (release) only after the attribute call
+  static std::atomic<int> max_clusters_dev[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  int scratch = 0;
-  int &max_clusters = (dev >= 0 && dev < 64) ? max_clusters_dev[dev] : scratch;
+  std::atomic<int> scratch{0};
+  std::atomic<int> &slot = (dev >= 0 && dev < 64) ? max_clusters_dev[dev] : scratch;
+  int max_clusters = slot.load(std::memory_order_acquire);
   auto kern = gemm_i8_2sm_kernel<G, B, SUB>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -443,6 +448,7 @@ static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, 
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = device_sms() / 2;
     max_clusters = n;
+    slot.store(n, std::memory_order_release);
   }
   const int64_t clusters = pair_tiles < max_clusters ? pair_tiles : max_clusters;
   cfg.gridDim = dim3((unsigned)(2 * clusters));

@@ -92,22 +92,59 @@ template <int V> struct StoreVec;
 template <> struct StoreVec<4> { using T = uint2; };
 template <> struct StoreVec<8> { using T = uint4; };
 
-// Stores token rows [m_begin, m_end) of a CTA's staged BF16 tile (128 columns from col0):
-// V columns per lane, so 128 / V lanes per row (V = 8: 16-byte stores, two rows per warp
-// instruction).  Dense: optional residual bf16(res + y), and copies to out_peer.  Grouped:
-// row scatter through perm, or the expert-parallel return bf16(value * probability) into
-// the route's home rank.
+// Where the rows a warp stores go (grouped mode), read before the tile's accumulator is
+// ready so the loads overlap the mainloop instead of sitting in front of every row store:
+// lane l holds row m_begin + l's output row (perm) and, for the expert-parallel return,
+// that route's probability, home rank and home row.
+struct RowDest {
+  int orow = 0, rank = 0, rrow = 0;
+  float prob = 0.0f;
+};
+
+template <bool GROUPED>
+CQ_DEV RowDest fetch_row_dest(const GemmParams &p, int64_t row0, int rows_valid, int m_begin, int m_end, int lane) {
+  RowDest d;
+  const int m = m_begin + lane;
+  if (GROUPED && m < m_end && m < rows_valid) {
+    const int64_t pos = row0 + m;
+    d.orow = p.scatter ? p.perm[pos] : (int)pos;
+    if (p.ret_row) {
+      d.prob = p.ret_prob[d.orow];
+      d.rank = p.ret_rank[d.orow];
+      d.rrow = p.ret_row[d.orow];
+    }
+  }
+  return d;
+}
+
+// Stores token rows [m_begin, m_end) (at most 32) of a CTA's staged BF16 tile (128 columns
+// from col0): V columns per lane, so 128 / V lanes per row (V = 8: 16-byte stores, two rows
+// per warp instruction).  Dense: optional residual bf16(res + y), and copies to out_peer.
+// Grouped: row scatter through perm, or the expert-parallel return bf16(value * probability)
+// into the route's home rank, with the destinations taken from dest (fetch_row_dest).
 template <bool GROUPED, int V>
 CQ_DEV void store_tile_rows(const GemmParams &p, const uint16_t *staging, int64_t row0, int rows_valid, int col0,
-                            int m_begin, int m_end, int lane) {
+                            int m_begin, int m_end, int lane, const RowDest &dest) {
   using Vec = typename StoreVec<V>::T;
   constexpr int LPR = 128 / V;  // lanes per row
   constexpr int RPI = 32 / LPR;  // rows per warp iteration
   const int sub = lane / LPR, l = lane % LPR;
-  for (int m = m_begin + sub; m < m_end && m < rows_valid; m += RPI) {
+  const int iters = (m_end - m_begin + RPI - 1) / RPI;  // the same on every lane
+  for (int it = 0; it < iters; ++it) {
+    const int mi = it * RPI + sub;  // row within [m_begin, m_end)
+    const int m = m_begin + mi;
+    int64_t orow = row0 + m;
+    float pr = 0.0f;
+    int rk = 0, rrow = 0;
+    if (GROUPED) {
+      // shuffles run on every lane (mi < 32), before the row checks
+      orow = __shfl_sync(0xffffffffu, dest.orow, mi & 31);
+      pr = __shfl_sync(0xffffffffu, dest.prob, mi & 31);
+      rk = __shfl_sync(0xffffffffu, dest.rank, mi & 31);
+      rrow = __shfl_sync(0xffffffffu, dest.rrow, mi & 31);
+    }
+    if (m >= m_end || m >= rows_valid) continue;
     const int64_t pos = row0 + m;
-    int64_t orow = pos;
-    if (GROUPED && p.scatter) orow = p.perm[pos];
     Vec v = *reinterpret_cast<const Vec *>(staging + m * 128 + V * l);
     uint16_t *hv = reinterpret_cast<uint16_t *>(&v);
     if (!GROUPED && p.residual) {
@@ -117,10 +154,9 @@ CQ_DEV void store_tile_rows(const GemmParams &p, const uint16_t *staging, int64_
       for (int q = 0; q < V; ++q) hv[q] = f32_to_bf16(__fadd_rn(bf16_to_f32(hr[q]), bf16_to_f32(hv[q])));
     }
     if (GROUPED && p.ret_row) {
-      const float pr = p.ret_prob[orow];
 #pragma unroll
       for (int q = 0; q < V; ++q) hv[q] = f32_to_bf16(__fmul_rn(bf16_to_f32(hv[q]), pr));
-      uint16_t *dst = p.ret_base[p.ret_rank[orow]] + (int64_t)p.ret_row[orow] * p.ldo + col0 + V * l;
+      uint16_t *dst = p.ret_base[rk] + (int64_t)rrow * p.ldo + col0 + V * l;
       *reinterpret_cast<Vec *>(dst) = v;
       continue;
     }
@@ -388,6 +424,9 @@ __global__ void __launch_bounds__(THREADS2, 1)
           }
         }
       }
+      // each warp stores 24 token rows of every sub-tile, 256 contiguous bytes per row
+      const int m0 = eidx * (BN2 / EPI_WARPS);
+      const RowDest dest = fetch_row_dest<GROUPED>(p, row0, rows_valid, m0, m0 + BN2 / EPI_WARPS, lane);
       int which, w_row_tile;
       weight_tile(np, expert, which, w_row_tile);
       const float ws = p.w_scales[which][(int64_t)w_row_tile * 128 + r];
@@ -458,10 +497,10 @@ __global__ void __launch_bounds__(THREADS2, 1)
         }
         if (GROUPED || !p.out_f32) {
           named_barrier_sync(1, 32 * EPI_WARPS);
-          // each warp stores 24 token rows, 256 contiguous bytes per row
-          const int m0 = eidx * (BN2 / EPI_WARPS);
-          if (p.store16) store_tile_rows<GROUPED, 8>(p, staging, srow0, svalid, col0, m0, m0 + BN2 / EPI_WARPS, lane);
-          else store_tile_rows<GROUPED, 4>(p, staging, srow0, svalid, col0, m0, m0 + BN2 / EPI_WARPS, lane);
+          if (p.store16)
+            store_tile_rows<GROUPED, 8>(p, staging, srow0, svalid, col0, m0, m0 + BN2 / EPI_WARPS, lane, dest);
+          else
+            store_tile_rows<GROUPED, 4>(p, staging, srow0, svalid, col0, m0, m0 + BN2 / EPI_WARPS, lane, dest);
           named_barrier_sync(1, 32 * EPI_WARPS);
         }
       }

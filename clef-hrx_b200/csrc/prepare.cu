@@ -17,6 +17,8 @@
 // 16 and 64 exchange partial sums/differences with xor-shuffles.  The reference's
 // operation order is kept (s01 = a+b, s23 = c+d, d01 = a-b, d23 = c-d; o = s01+d23,
 // s01-d23, d01+s23, s23-d01), bit-identical under IEEE round-to-nearest-even.
+#include <atomic>
+
 #include "cq_common.cuh"
 #include "clefq_internal.h"
 
@@ -689,26 +691,28 @@ size_t max_smem_bytes() {
 
 template <int CH, int KIND>
 int resident_ctas(int threads, size_t smem) {
-  static int cache[kMaxDevices][17];
-  static bool attr[kMaxDevices];
+  // Filled on first use by whichever host thread gets there; concurrent fillers compute the
+  // same values, and the release/acquire pair orders the attribute call before its flag.
+  static std::atomic<int> cache[kMaxDevices][17];
+  static std::atomic<bool> attr[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
   const int warps = threads / 32 > 16 ? 16 : threads / 32;
   if (dev < 0 || dev >= kMaxDevices) return 1;
-  if (!attr[dev]) {
+  if (!attr[dev].load(std::memory_order_acquire)) {
     const size_t most = max_smem_bytes<CH, KIND>();
     if (most > 48 * 1024)
       cudaFuncSetAttribute(prepare_kernel<CH, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most);
-    attr[dev] = true;
+    attr[dev].store(true, std::memory_order_release);
   }
-  if (!cache[dev][warps]) {
-    int n = 0;
+  int n = cache[dev][warps].load(std::memory_order_relaxed);
+  if (!n) {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, prepare_kernel<CH, KIND>, threads, smem) != cudaSuccess ||
         n <= 0)
       n = 1;
-    cache[dev][warps] = n;
+    cache[dev][warps].store(n, std::memory_order_relaxed);
   }
-  return cache[dev][warps];
+  return n;
 }
 
 template <int CH, int KIND>
@@ -740,14 +744,14 @@ bool launch_kind(int ch, const PrepareArgs &a, int threads, size_t smem, int64_t
 namespace {
 template <int NS, bool TAB>
 void launch_pack(const PrepareArgs &a, int threads, size_t smem, int64_t nblk, cudaStream_t stream) {
-  static bool attr[kMaxDevices];
+  static std::atomic<bool> attr[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDevices || !attr[dev]) {
+  if (dev < 0 || dev >= kMaxDevices || !attr[dev].load(std::memory_order_acquire)) {
     // largest request of this instance: table + maxima + the stage budget
     const int most = (TAB ? kSiluEntries * 2 : 0) + kPackRedBytes + (TAB ? 96 : 128) * 1024;
     cudaFuncSetAttribute(pack_kernel<NS, TAB>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
-    if (dev >= 0 && dev < kMaxDevices) attr[dev] = true;
+    if (dev >= 0 && dev < kMaxDevices) attr[dev].store(true, std::memory_order_release);
   }
   int64_t grid = device_sms();
   if (grid > nblk) grid = nblk;
