@@ -273,9 +273,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
       uint32_t g = 0;
       int i = 0;
       bool ok = true;
-      int64_t row0;
-      int rows_valid, np, expert;
-      for (int t = cluster; ok && tm.get(p, t, row0, rows_valid, np, expert); t += nclusters, ++i) {
+      // the issuer needs only the tile count: no tile-list loads on its chain
+      for (int t = cluster; ok && t < tm.total; t += nclusters, ++i) {
         // SUB = 1: accumulator buffer i & 1 (double buffered); SUB = 2: both buffers, one
         // per sub-tile, released together by the epilogue
         const int buf = SUB == 1 ? (i & 1) : 0;
@@ -318,9 +317,9 @@ __global__ void __launch_bounds__(THREADS2, 1)
     const uint32_t lead_sink = mapa_shared(smem_u32(&s.sink[warp]), 0);
     uint32_t g = 0;
     bool ok = true;
-    int64_t row0;
-    int rows_valid, np, expert;
-    for (int t = cluster; ok && tm.get(p, t, row0, rows_valid, np, expert); t += nclusters) {
+    // the converters convert whatever weight block the producer loaded: the tile count is
+    // all they need (no tile-list loads on the per-stage chain)
+    for (int t = cluster; ok && t < tm.total; t += nclusters) {
       for (int kb = 0; kb < k_stages; ++kb, ++g) {
         const int st = g % NW;
         const int sw = g % NSW;
