@@ -502,17 +502,21 @@ CQ_DEV void bf16r2_inplace(float &lo, float &hi) {
 }
 
 // The same combine with topk fixed at compile time: the K route rows' 16-byte chunks are all
-// loaded before the ordered chain consumes them, so a thread has K loads in flight instead
-// of one.  Identical arithmetic and order to combine_kernel.
-template <int K, bool WEIGHTED>
+// loaded before the ordered chain consumes them, so a thread has K x CPT / 8 loads in flight
+// instead of one.  CPT = 16 columns per thread (two chunks per route row) when the width
+// allows it.  The route rows are read once, so their loads stream past the caches (ld.cs);
+// measured on the C4 combine this took 62.5 -> 55.6 us.  Identical arithmetic and order to
+// combine_kernel.
+template <int K, bool WEIGHTED, int CPT>
 __global__ void combine_k_kernel(const uint16_t *__restrict__ values, const float *__restrict__ routes,
                                  const float *__restrict__ order, int64_t tokens, int64_t width,
                                  uint16_t *__restrict__ out) {
-  const int64_t per_tok = width / 8;
+  constexpr int NV = CPT / 8;  // 16-byte chunks per route row and thread
+  const int64_t per_tok = width / CPT;
   const int64_t total = tokens * per_tok;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = i / per_tok;
-    const int64_t c = (i % per_tok) * 8;
+    const int64_t c = (i % per_tok) * CPT;
     const float *rt = routes + t * 2 * K;
     int rank[K];
     if (order) {
@@ -539,41 +543,51 @@ __global__ void combine_k_kernel(const uint16_t *__restrict__ values, const floa
         rank[j] = r;
       }
     }
-    uint4 raw[K];
+    uint4 raw[K][NV];
 #pragma unroll
-    for (int j = 0; j < K; ++j) raw[j] = *reinterpret_cast<const uint4 *>(values + (t * K + rank[j]) * width + c);
+    for (int j = 0; j < K; ++j)
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+        raw[j][v] = __ldcs(reinterpret_cast<const uint4 *>(values + (t * K + rank[j]) * width + c + 8 * v));
     // s = bf16(s + bf16(v * p)) with both roundings done two lanes at a time by
     // cvt.rn.bf16x2 (round to nearest even, as f32_to_bf16 for every finite value and
     // for infinities; a NaN stays a NaN).
-    float s[8];
+    float s[CPT];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) s[q] = 0.0f;
+    for (int q = 0; q < CPT; ++q) s[q] = 0.0f;
 #pragma unroll
     for (int j = 0; j < K; ++j) {
       const float p = rt[K + rank[j]];
-      const uint32_t *hw = reinterpret_cast<const uint32_t *>(&raw[j]);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float lo = __uint_as_float(hw[q] << 16);
-        float hi = __uint_as_float(hw[q] & 0xffff0000u);
-        if (!WEIGHTED) {
-          lo = __fmul_rn(lo, p);
-          hi = __fmul_rn(hi, p);
+      for (int v = 0; v < NV; ++v) {
+        const uint32_t *hw = reinterpret_cast<const uint32_t *>(&raw[j][v]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float lo = __uint_as_float(hw[q] << 16);
+          float hi = __uint_as_float(hw[q] & 0xffff0000u);
+          if (!WEIGHTED) {
+            lo = __fmul_rn(lo, p);
+            hi = __fmul_rn(hi, p);
+            bf16r2_inplace(lo, hi);
+          }
+          float &s0 = s[8 * v + 2 * q], &s1 = s[8 * v + 2 * q + 1];
+          lo = __fadd_rn(s0, lo);
+          hi = __fadd_rn(s1, hi);
           bf16r2_inplace(lo, hi);
+          s0 = lo;
+          s1 = hi;
         }
-        lo = __fadd_rn(s[2 * q], lo);
-        hi = __fadd_rn(s[2 * q + 1], hi);
-        bf16r2_inplace(lo, hi);
-        s[2 * q] = lo;
-        s[2 * q + 1] = hi;
       }
     }
-    uint4 o;
-    uint32_t *ow = reinterpret_cast<uint32_t *>(&o);
 #pragma unroll
-    for (int q = 0; q < 4; ++q)  // the sums are BF16 values already: keep their top halves
-      ow[q] = __byte_perm(__float_as_uint(s[2 * q]), __float_as_uint(s[2 * q + 1]), 0x7632);
-    *reinterpret_cast<uint4 *>(out + t * width + c) = o;
+    for (int v = 0; v < NV; ++v) {
+      uint4 o;
+      uint32_t *ow = reinterpret_cast<uint32_t *>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)  // the sums are BF16 values already: keep their top halves
+        ow[q] = __byte_perm(__float_as_uint(s[8 * v + 2 * q]), __float_as_uint(s[8 * v + 2 * q + 1]), 0x7632);
+      *reinterpret_cast<uint4 *>(out + t * width + c + 8 * v) = o;
+    }
   }
 }
 
@@ -585,9 +599,17 @@ int launch_combine(const uint16_t *values, const float *routes, const float *ord
   if (total == 0) return 0;
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
+  if (topk == 8 && width % 16 == 0) {
+    // 16 columns per thread, 128 threads per block, one block per 2048 columns of a token
+    const int64_t b16 = (tokens * (width / 16) + 127) / 128, cap16 = (int64_t)num_sms * 64;
+    const unsigned g16 = (unsigned)(b16 < cap16 ? b16 : cap16);
+    if (weighted) combine_k_kernel<8, true, 16><<<g16, 128, 0, stream>>>(values, routes, order, tokens, width, out);
+    else combine_k_kernel<8, false, 16><<<g16, 128, 0, stream>>>(values, routes, order, tokens, width, out);
+    return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  }
 #define CQ_COMBINE_K(K)                                                                            \
-  (weighted ? combine_k_kernel<K, true><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out) \
-            : combine_k_kernel<K, false><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out))
+  (weighted ? combine_k_kernel<K, true, 8><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out) \
+            : combine_k_kernel<K, false, 8><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out))
   switch (topk) {
     case 8: CQ_COMBINE_K(8); break;
     case 4: CQ_COMBINE_K(4); break;

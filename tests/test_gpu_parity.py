@@ -380,11 +380,12 @@ def test_expert_matches_oracle(cq, tokens, skewed, routed, k, n):
 
 
 @pytest.mark.parametrize("ordered", [True, False])
-@pytest.mark.parametrize("tokens", [1, 37, 513])
-def test_combine(cq, ordered, tokens):
+@pytest.mark.parametrize("tokens,width", [(1, 2048), (37, 2048), (513, 2048), (37, 264)])
+def test_combine(cq, ordered, tokens, width):
+    """Top-8 combine, bit-exact: 16 columns per thread when the width is a multiple of 16,
+    8 otherwise (width 264)."""
     from tests.golden.make_golden import expert_routes
     rng = np.random.default_rng(tokens)
-    width = 2048
     routes = expert_routes(tokens, False, 1)
     routes[:, 8:] = o.bf16_to_f32(o.f32_to_bf16(rng.random((tokens, 8)).astype(np.float32)))
     values = bf16_normal(rng, (tokens * 8, width))
