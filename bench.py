@@ -319,7 +319,7 @@ def run_clefq(args, world, rank, local):
     # and output copy, ~1.3 ms together) are spread as a serving loop spreads them.
     x_host = x.cpu().pin_memory()
     out_host = torch.empty((M, HIDDEN), dtype=torch.bfloat16).pin_memory()
-    e2e_steps = max(100, min(args.steps, 200))
+    e2e_steps = args.e2e_steps if args.e2e_steps > 0 else max(100, min(args.steps, 200))
     stream = torch.cuda.current_stream()
     best = None
     for chunk in (1024, 2048, 4096):
@@ -498,6 +498,9 @@ def main():
     ap.add_argument("--skip-moe", action="store_true")
     ap.add_argument("--skip-tp", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=0,
+                    help="calls in the timed e2e stream (default: --steps clamped to [100, 200]); "
+                         "small values keep profiler captures short")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

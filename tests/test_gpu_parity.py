@@ -430,3 +430,42 @@ def test_moe_block(cq, tokens):
         assert same_bits_f32(routes_out.cpu().numpy(), ref_routes)
         assert np.array_equal(from_dev_bf16(out), ref)
     cq.status()
+
+
+def test_calls_from_threads_on_own_streams(cq):
+    """The C ABI is reentrant on different streams: four host threads, each on its own CUDA
+    stream, run projections of different shapes (two-sub-tile, one-sub-tile and one-CTA GEMM
+    kernels, int4 and int8) at the same time; every result equals the oracle."""
+    import threading
+    cases = [(400, 512, 1024, 4), (37, 256, 512, 4), (65, 128, 2048, 4), (200, 256, 1024, 8)]
+    prepared = []
+    for m, n, k, bits in cases:
+        rng = np.random.default_rng(m * 7 + n + bits)
+        _, wt, ws, wdev = _weight(rng, n, k, bits)
+        x = bf16_normal(rng, (m, k))
+        _, ocodes, oscales, _ = o.prepare(x, bits, o.stride_for(k, bits))
+        prepared.append((x, wdev, bits, o.gemm(ocodes, oscales, wt, ws, n, k, bits=bits)))
+    results = [None] * len(cases)
+    errors = []
+
+    def work(i):
+        try:
+            x, wdev, bits, _ = prepared[i]
+            stream = torch.cuda.Stream()
+            with torch.cuda.stream(stream):
+                xd = to_dev_bf16(x)
+                outs = [cq.project_quantized(xd, wdev) for _ in range(5)]
+            stream.synchronize()
+            results[i] = [from_dev_bf16(t) for t in outs]
+        except Exception as e:  # reported on the main thread
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(len(cases))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for (_, _, _, ref), outs in zip(prepared, results):
+        for got in outs:
+            assert np.array_equal(got, ref)
