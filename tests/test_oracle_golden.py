@@ -203,3 +203,93 @@ def test_exp_error_bound():
     assert np.isinf(o.exp(np.array([89.0], np.float32))[0])
     assert o.exp(np.array([-104.0], np.float32))[0] == 0
     assert np.isnan(o.exp(np.array([np.nan], np.float32))[0])
+
+
+def _norm_case_values(rows, width):
+    """The input rows of src/quantized.rs:1553-1774: a (rows + 2) x width array whose row
+    class (i / width) % 11 selects signed zeros, tiny, BF16 MAX, subnormal, huge, NaN/+Inf/-Inf
+    at one column, +-1 or scaled ramp values; the packed rows are 1 .. rows."""
+    i = np.arange((rows + 2) * width, dtype=np.int64)
+    c, cls = i % width, (i // width) % 11
+    value = ((i * 37 % 1031).astype(np.float32) - np.float32(515)) / np.float32(37)
+    v = value.copy()
+    v[cls == 0] = np.where(c[cls == 0] % 2 == 0, np.float32(0.0), np.float32(-0.0))
+    v[cls == 1] = value[cls == 1] * np.float32(1e-5)
+    v[cls == 2] = o.bf16_to_f32(np.uint16(0x7F7F))
+    v[cls == 3] = o.bf16_to_f32(np.uint16(1))
+    v[cls == 4] = value[cls == 4] * np.float32(1e15)
+    v[(cls == 5) & (c == 37)] = np.nan
+    v[(cls == 6) & (c == 113)] = np.inf
+    v[(cls == 7) & (c == 259)] = -np.inf
+    v[cls == 8] = np.where(c[cls == 8] % 2 == 0, np.float32(1.0), np.float32(-1.0))
+    v[cls == 9] = value[cls == 9] * np.float32(1e-3)
+    return o.f32_to_bf16(v.astype(np.float32)).reshape(rows + 2, width)
+
+
+def _norm_case_weight(width, exceptional):
+    i = np.arange(3 * width, dtype=np.int64)
+    if exceptional:
+        w = np.full(i.shape, 0.5, np.float32)
+        w[i % 1009 == 0] = np.nan
+        w[i % 1009 == 1] = np.inf
+        w[i % 1009 == 2] = -np.inf
+        w[i % 1009 == 3] = o.bf16_to_f32(np.uint16(0x7F7F))
+    else:
+        w = ((i * 13 % 127).astype(np.float32) - np.float32(63)) / np.float32(128)
+        w[i % 19 == 0] = -1.0
+        w[i % 19 == 1] = -0.0
+        w[i % 19 == 2] = 0.0
+    return o.f32_to_bf16(w.astype(np.float32))[2 * width:]
+
+
+def _bf16_ulp(a, b):
+    def ordered(h):
+        h = h.astype(np.int64)
+        return np.where(h & 0x8000, (~h) & 0xFFFF, h | 0x8000)
+    return np.abs(ordered(a) - ordered(b))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("exceptional_weight", [False, True])
+@pytest.mark.parametrize("rows", [1, 7, 65, 158])
+def test_norm_packing_known_answers(bits, exceptional_weight, rows):
+    """src/quantized.rs:1553-1774 on the oracle (width 5120): packing with the RMSNorm stored
+    gives the same codes and scales as without storing; packing the stored normalised rows
+    separately stays within the reference's bounds of the fused codes (|delta| <= 1 on at most
+    1% of codes, scales within 0.4%; here they are equal, since the fused packing quantises the
+    BF16 normalised values); and on finite rows without subnormal inputs every normalised value
+    is within one BF16 step of the reference's FP64 RMS oracle."""
+    width = 5120
+    values = _norm_case_values(rows, width)
+    x = values[1:rows + 1]
+    w = _norm_case_weight(width, exceptional_weight)
+    stride = width + 512 // bits
+    fused, fcodes, fscales, _ = o.prepare(x, bits, stride, o.NORM, w)
+    stored, _, sscales, norm = o.prepare(x, bits, stride, o.NORM_STORE, w)
+    assert np.array_equal(fused, stored)
+    _, ucodes, uscales, _ = o.prepare(norm, bits, stride)
+    p = 32 // bits
+    for lane in range(p):
+        def dec(words):
+            return ((words[:, : width // p] << np.uint32(32 - bits * (lane + 1))).view(np.int32)
+                    >> np.int32(32 - bits))
+        assert np.abs(dec(fcodes) - dec(ucodes)).max() <= 1
+    assert np.array_equal(_logical(fcodes, width, bits), _logical(ucodes, width, bits))
+    finite = np.isfinite(uscales)
+    assert np.array_equal(fscales[~finite].view(np.uint32), uscales[~finite].view(np.uint32))
+    assert np.all(np.abs(fscales[finite] - uscales[finite]) <= np.maximum(np.abs(uscales[finite]), 1e-30) * 0.004)
+    if exceptional_weight:
+        return
+    wf = (o.bf16_to_f32(w) + np.float32(1.0)).astype(np.float64)
+    checked = 0
+    for row in sorted({0, rows // 2, rows - 1}):
+        v = o.bf16_to_f32(x[row])
+        if not (np.all(np.isfinite(v)) and np.all(np.abs(v) <= 1e16)
+                and np.all((v == 0) | (np.abs(v) >= np.finfo(np.float32).tiny))):
+            continue
+        vd = v.astype(np.float64)
+        inv = 1.0 / np.sqrt(np.sum(vd * vd) / width + np.float64(np.float32(1e-6)))
+        ref = o.f32_to_bf16((vd * inv * wf).astype(np.float32))
+        assert _bf16_ulp(norm[row], ref).max() <= 1, row
+        checked += 1
+    assert rows < 7 or checked > 0
