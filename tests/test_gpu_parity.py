@@ -469,3 +469,28 @@ def test_calls_from_threads_on_own_streams(cq):
     for (_, _, _, ref), outs in zip(prepared, results):
         for got in outs:
             assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("m,k,n,padded", [(33, 1024, 256, True), (7, 512, 128, False), (65, 2048, 384, True)])
+@pytest.mark.parametrize("varying", [False, True])
+def test_gemm_exact_benchmark_inputs(cq, bits, m, k, n, padded, varying):
+    """The reference's packed integer GEMM benchmark fixture (src/benchmarking.rs:190-197,
+    286-410) through clefq_gemm: raw codes (int4 codes include -8, which prepared rows never
+    hold), uniform or varying row scales with zero rows; bit-exact to the oracle."""
+    from tests.test_oracle_golden import _bench_codes, _bench_scales
+    stride = k + (512 // bits if padded and k % 1024 == 0 else 0)
+    _, a_words = _bench_codes(m, k, bits, stride)
+    _, w_words = _bench_codes(n, k, bits, stride)
+    a_s = _bench_scales(m, bits, 3, 17, varying)
+    w_s = _bench_scales(n, bits, 7, 23, varying)
+    w_tiled = o.retile(w_words, n, k, bits)
+    ref = o.gemm(a_words, a_s, w_tiled, w_s, n, k, bits=bits)
+    words = stride // (32 // bits)
+    storage = to_dev(np.concatenate([a_words.ravel().view(np.int32), a_s.view(np.int32)]))
+    a = cq.Prepared(storage, storage[: m * words].view(m, words), storage[m * words:].view(torch.float32), None, None,
+                    bits, stride)
+    wdev = cq.QuantizedWeight(to_dev(w_tiled.view(np.int32)), to_dev(w_s), n, k, stride, bits)
+    for _ in range(2):
+        out = cq.project_prepared(m, wdev, a)
+        assert np.array_equal(from_dev_bf16(out), ref)

@@ -293,3 +293,60 @@ def test_norm_packing_known_answers(bits, exceptional_weight, rows):
         assert _bf16_ulp(norm[row], ref).max() <= 1, row
         checked += 1
     assert rows < 7 or checked > 0
+
+
+def _bench_codes(rows, k, bits, stride):
+    """The packed integer GEMM fixture of src/benchmarking.rs:190-197,351-364: element i of a
+    row-major rows x k matrix is gemm_value(i) = ((i * 17 % 251) - 125) / 128, for int4 rounded
+    (half away from zero, as Rust's round) to eighths in [-8, 7] / 8; divided by the uniform
+    scale it is an exact code, packed little-endian, code c at bits (c % P) * bits of word c / P.
+    Returns (codes as int64, packed words [rows][stride / P])."""
+    i = np.arange(rows * k, dtype=np.int64).reshape(rows, k)
+    value = ((i * 17 % 251).astype(np.float32) - np.float32(125)) / np.float32(128)
+    if bits == 4:
+        t = value * np.float32(8)
+        code = np.clip(np.sign(t) * np.floor(np.abs(t) + np.float32(0.5)), -8, 7).astype(np.int64)
+    else:
+        code = (value * np.float32(128)).astype(np.int64)
+    p = 32 // bits
+    nib = (code & ((1 << bits) - 1)).astype(np.uint64).reshape(rows, k // p, p)
+    words = np.zeros((rows, stride // p), np.uint32)
+    words[:, : k // p] = (nib << (np.arange(p, dtype=np.uint64) * bits)).sum(axis=2).astype(np.uint32)
+    return code, words
+
+
+def _bench_scales(rows, bits, factor, zero_period, varying):
+    if not varying:
+        return np.full(rows, 1.0 / (1 << (bits - 1)), np.float32)
+    r = np.arange(rows, dtype=np.int64)
+    s = ((r * factor % 31 + 1).astype(np.float32) / np.float32(257.0)) * np.exp2(
+        -((r * factor % 5) * 4).astype(np.float32))
+    s[r % zero_period == 0] = 0.0
+    return s.astype(np.float32)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("m,k,n,padded", [(33, 1024, 256, True), (7, 512, 128, False), (65, 2048, 384, True)])
+@pytest.mark.parametrize("varying", [False, True])
+def test_gemm_exact_benchmark_inputs(bits, m, k, n, padded, varying):
+    """The reference's packed integer GEMM benchmark inputs (src/benchmarking.rs:286-410):
+    codes that are exact (int4 codes include -8), uniform scales 1/8 or 1/128, or the
+    CLEF_BENCH_INTEGER_ROW_SCALES variant (zero rows, scales down to 2^-16).  The oracle's int32
+    accumulators equal the exact integer dot, and its BF16 outputs equal the epilogue
+    (f32(acc) * ws) * as rounded once; with uniform scales the product before rounding is
+    exact."""
+    stride = k + (512 // bits if padded and k % 1024 == 0 else 0)
+    a_code, a_words = _bench_codes(m, k, bits, stride)
+    w_code, w_words = _bench_codes(n, k, bits, stride)
+    a_s = _bench_scales(m, bits, 3, 17, varying)
+    w_s = _bench_scales(n, bits, 7, 23, varying)
+    w_tiled = o.retile(w_words, n, k, bits)
+    out, acc = o.gemm(a_words, a_s, w_tiled, w_s, n, k, bits=bits, want_acc=True)
+    exact = a_code @ w_code.T
+    assert np.array_equal(acc.astype(np.int64), exact)
+    y = (exact.astype(np.float32) * w_s[None, :]) * a_s[:, None] + np.float32(0.0)
+    big = o.bf16_to_f32(np.uint16(0x7F7F))
+    y = np.where(np.isfinite(y), np.clip(y, -big, big), y).astype(np.float32)
+    assert np.array_equal(out, o.f32_to_bf16(y))
+    if not varying:
+        assert np.array_equal(y.astype(np.float64), exact.astype(np.float64) * (a_s[0] * np.float64(w_s[0])))
