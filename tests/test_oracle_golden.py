@@ -350,3 +350,36 @@ def test_gemm_exact_benchmark_inputs(bits, m, k, n, padded, varying):
     assert np.array_equal(out, o.f32_to_bf16(y))
     if not varying:
         assert np.array_equal(y.astype(np.float64), exact.astype(np.float64) * (a_s[0] * np.float64(w_s[0])))
+
+
+def _swiglu_case(rows, width):
+    """The gate and up rows of src/quantized.rs:1187-1266: gate row class (i / width) % 7 gives
+    zeros, one NaN (column 259), one +Inf (column 515), BF16 MAX, a BF16 subnormal, +-80, or a
+    ramp; up is a ramp; the packed rows are gate rows 1 .. rows and up rows 2 .. rows + 1."""
+    i = np.arange((rows + 2) * width, dtype=np.int64)
+    col, cls = i % width, (i // width) % 7
+    g = ((i * 17 % 1031).astype(np.float32) - np.float32(515)) / np.float32(16)
+    g[cls == 0] = 0.0
+    g[(cls == 1) & (col == 259)] = np.nan
+    g[(cls == 2) & (col == 515)] = np.inf
+    g[cls == 3] = o.bf16_to_f32(np.uint16(0x7F7F))
+    g[cls == 4] = np.uint32(0x00010000).view(np.float32)
+    g[cls == 5] = np.where(col[cls == 5] % 2 == 0, np.float32(-80.0), np.float32(80.0))
+    j = np.arange((rows + 3) * width, dtype=np.int64)
+    u = ((j * 29 % 997).astype(np.float32) - np.float32(498)) / np.float32(32)
+    gate = o.f32_to_bf16(g.astype(np.float32)).reshape(rows + 2, width)[1:rows + 1]
+    up = o.f32_to_bf16(u.astype(np.float32)).reshape(rows + 3, width)[2:rows + 2]
+    return np.ascontiguousarray(gate), np.ascontiguousarray(up)
+
+
+@pytest.mark.parametrize("width,bits,rows", [(17408, 4, 1), (17408, 4, 158), (17408, 8, 128), (17408, 8, 620),
+                                             (768, 4, 8), (768, 4, 136), (768, 4, 2048), (768, 4, 16384)])
+def test_fused_swiglu_packing_equals_separate(width, bits, rows):
+    """src/quantized.rs:1187-1266: packing with SwiGLU fused in gives the same code words and
+    scale bits as SwiGLU followed by plain packing, on the reference's exceptional rows."""
+    gate, up = _swiglu_case(rows, width)
+    stride = width + 512 // bits
+    _, fcodes, fscales, _ = o.prepare(gate, bits, stride, o.SWIGLU, up)
+    _, scodes, sscales, _ = o.prepare(o.swiglu(gate, up), bits, stride)
+    assert np.array_equal(_logical(fcodes, width, bits), _logical(scodes, width, bits))
+    assert np.array_equal(fscales.view(np.uint32), sscales.view(np.uint32))
