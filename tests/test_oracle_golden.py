@@ -383,3 +383,39 @@ def test_fused_swiglu_packing_equals_separate(width, bits, rows):
     _, scodes, sscales, _ = o.prepare(o.swiglu(gate, up), bits, stride)
     assert np.array_equal(_logical(fcodes, width, bits), _logical(scodes, width, bits))
     assert np.array_equal(fscales.view(np.uint32), sscales.view(np.uint32))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("rows", [1, 128, 158, 620])
+def test_attention_gate_packing_equals_separate(bits, rows):
+    """src/quantized.rs:1268-1368 (width 6144, 24 heads): packing with the sigmoid attention
+    gate fused in equals the separate steps -- gate columns 512h + 256 .. 512h + 511 of the
+    q|gate rows, s = bf16(1 / (1 + exp(-g))), v = bf16(a * s), plain packing -- bit for bit,
+    while every Q half of the q|gate rows is NaN and must not be read."""
+    width = 6144
+    i = np.arange((rows + 2) * width, dtype=np.int64)
+    cls = (i // width) % 7
+    a = ((i * 29 % 997).astype(np.float32) - np.float32(498)) / np.float32(32)
+    a[cls == 0] = 0.0
+    a[cls == 3] = o.bf16_to_f32(np.uint16(0x7F7F))
+    attn = o.f32_to_bf16(a).reshape(rows + 2, width)[1:rows + 1].copy()
+    j = np.arange((rows + 3) * width * 2, dtype=np.int64)
+    col, qc = j % (2 * width), (j // (2 * width)) % 7
+    q = ((j * 17 % 1031).astype(np.float32) - np.float32(515)) / np.float32(16)
+    q[qc == 0] = 0.0
+    q[(qc == 1) & (col == 771)] = np.nan
+    q[(qc == 2) & (col == 1283)] = np.inf
+    q[qc == 3] = o.bf16_to_f32(np.uint16(0x7F7F))
+    q[qc == 4] = np.uint32(0x00010000).view(np.float32)
+    q[qc == 5] = np.where(col[qc == 5] % 2 == 0, np.float32(-80.0), np.float32(80.0))
+    q[col % 512 < 256] = np.nan
+    q_gate = o.f32_to_bf16(q.astype(np.float32)).reshape(rows + 3, 2 * width)[2:rows + 2].copy()
+    stride = width + 512 // bits
+    _, fcodes, fscales, _ = o.prepare(attn, bits, stride, o.ATTN_GATE, q_gate)
+    gate = o.bf16_to_f32(q_gate.reshape(rows, 24, 512)[:, :, 256:].reshape(rows, width))
+    with np.errstate(all="ignore"):
+        s = o.f32_to_bf16(np.float32(1.0) / (np.float32(1.0) + o.exp(-gate).astype(np.float32)))
+        v = o.f32_to_bf16(o.bf16_to_f32(attn) * o.bf16_to_f32(s))
+    _, scodes, sscales, _ = o.prepare(v, bits, stride)
+    assert np.array_equal(_logical(fcodes, width, bits), _logical(scodes, width, bits))
+    assert np.array_equal(fscales.view(np.uint32), sscales.view(np.uint32))
