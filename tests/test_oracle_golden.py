@@ -419,3 +419,47 @@ def test_attention_gate_packing_equals_separate(bits, rows):
     _, scodes, sscales, _ = o.prepare(v, bits, stride)
     assert np.array_equal(_logical(fcodes, width, bits), _logical(scodes, width, bits))
     assert np.array_equal(fscales.view(np.uint32), sscales.view(np.uint32))
+
+
+@pytest.mark.parametrize("k,rows", [(6144, 127), (6144, 129), (6144, 257), (17408, 129)])
+def test_residual_projection_equals_separate_addition(k, rows):
+    """src/quantized.rs:1409-1552 (n 5120): the residual-fused projection equals the plain
+    projection followed by bf16(residual + y), bit for bit (NaN as NaN), with zero and 1e34
+    weight scales, zero activation scales and NaN/Inf/MAX/-0/subnormal residuals."""
+    n = 5120
+    stride = k + (128 if k % 1024 == 0 else 0)
+    words = stride // 8
+
+    def packed(r):
+        row = np.arange(r, dtype=np.int64)[:, None, None]
+        word = np.arange(k // 8, dtype=np.int64)[None, :, None]
+        lane = np.arange(8, dtype=np.int64)[None, None, :]
+        code = (row * 17 + word * 7 + lane * 3) % 15 - 7
+        data = np.zeros((r, words), np.uint32)
+        data[:, : k // 8] = ((code & 15).astype(np.uint64) << (lane.astype(np.uint64) * 4)).sum(axis=2)
+        return data
+
+    w_codes = packed(n + 1)[1:]
+    i = np.arange(n + 3)
+    ws = np.where(i % 23 == 0, 0.0, np.where(i % 29 == 0, 1e34, (i % 31 + 1) / 257.0)).astype(np.float32)[3:]
+    a_codes = packed(rows + 2)[2:]
+    i = np.arange(rows + 2)
+    a_s = np.where(i % 17 == 0, 0.0, (i % 19 + 1) / 131.0).astype(np.float32)[2:]
+    i = np.arange((rows + 1) * n, dtype=np.int64)
+    r = ((i * 43 % 997).astype(np.float32) - np.float32(498)) / np.float32(257)
+    big = o.bf16_to_f32(np.uint16(0x7F7F))
+    for idx, val in enumerate([np.nan, np.inf, -np.inf, big, -big, -0.0, 0.0, o.bf16_to_f32(np.uint16(1))]):
+        r[i % 1009 == idx] = val
+    residual = o.f32_to_bf16(r.astype(np.float32)).reshape(rows + 1, n)[1:].copy()
+    w_tiled = o.retile(w_codes, n, k, 4)
+    plain = o.gemm(a_codes, a_s, w_tiled, ws, n, k)
+    fused = o.gemm(a_codes, a_s, w_tiled, ws, n, k, residual=residual)
+    with np.errstate(all="ignore"):
+        expected = o.f32_to_bf16(o.bf16_to_f32(residual) + o.bf16_to_f32(plain))
+    nan = np.isnan(o.bf16_to_f32(expected))
+    assert np.array_equal(np.isnan(o.bf16_to_f32(fused)), nan)
+    assert np.array_equal(fused[~nan], expected[~nan])
+    # the 1e34 weight scales reach huge outputs (and inf * 0 = NaN where they overflow on a row
+    # whose activation scale is zero, as the epilogue order (acc * ws) * as gives)
+    pf = o.bf16_to_f32(plain)
+    assert np.nanmax(np.abs(pf)) > 1e35 and (pf == 0).any()
