@@ -463,3 +463,19 @@ def test_residual_projection_equals_separate_addition(k, rows):
     # whose activation scale is zero, as the epilogue order (acc * ws) * as gives)
     pf = o.bf16_to_f32(plain)
     assert np.nanmax(np.abs(pf)) > 1e35 and (pf == 0).any()
+
+
+def test_golden_file_regenerates_from_its_script(golden):
+    """tests/golden/golden.npz is exactly what tests/golden/make_golden.py produces: every
+    array, regenerated in memory, equals the committed one (dtype, shape and bits)."""
+    from tests.golden import make_golden as mg
+    out = {}
+    with np.errstate(all="ignore"):
+        for cases in (mg.packing_cases, mg.exceptional_cases, mg.gemm_cases, mg.route_cases, mg.group_cases):
+            cases(out)
+    assert sorted(out) == sorted(golden)
+    for name, arr in out.items():
+        ref = golden[name]
+        arr = np.asarray(arr)
+        assert arr.dtype == ref.dtype and arr.shape == ref.shape, name
+        assert arr.tobytes() == ref.tobytes(), name
