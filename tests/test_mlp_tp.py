@@ -74,6 +74,11 @@ def test_tp_host_logic_two_gloo_ranks():
     mp.start_processes(_cpu_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
 
 
+def test_tp_host_logic_four_gloo_ranks():
+    """Four ranks: one 256-group of the intermediate and 128 output columns per rank."""
+    mp.start_processes(_cpu_worker, args=(4, _free_port()), nprocs=4, join=True, start_method="spawn")
+
+
 # ---------------------------------------------------------------------------------------
 # GPU
 # ---------------------------------------------------------------------------------------

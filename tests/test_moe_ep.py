@@ -1,6 +1,6 @@
 """Expert-parallel Omni MoE: every rank's output equals the single-GPU layer bit for bit.
 
-- CPU, 2 gloo ranks: the real host orchestration (clefq.ep.omni_moe_ep) with the device
+- CPU, 2 and 4 gloo ranks: the real host orchestration (clefq.ep.omni_moe_ep) with the device
   steps replaced by oracle stand-ins, against the oracle's single-process moe_layer
   (src/omni.rs:761-857 semantics).
 - GPU, one process: G = 2 and 4 ranks simulated by splicing send/receive buffers exactly as
@@ -35,10 +35,9 @@ def _free_port():
 CPU_T, CPU_H, CPU_I, CPU_E, CPU_K = 24, 256, 256, 8, 2
 
 
-def _cpu_problem():
+def _cpu_problem(world):
     from oracle import oracle as o
     rng = np.random.default_rng(7)
-    world = 2
     x = o.f32_to_bf16(rng.standard_normal((world * CPU_T, CPU_H)).astype(np.float32))
     logits = o.f32_to_bf16(rng.standard_normal((world * CPU_T, CPU_E)).astype(np.float32))
     gate = o.pack_weight(o.f32_to_bf16(rng.standard_normal((CPU_E * CPU_I, CPU_H)).astype(np.float32) * 0.05))
@@ -55,7 +54,7 @@ def _cpu_worker(rank, world, port):
     from tests.ep_oracle_ops import OracleEpOps
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
-        x, logits, gate, up, down = _cpu_problem()
+        x, logits, gate, up, down = _cpu_problem(world)
         per = CPU_E // world
         base = rank * per
 
@@ -81,6 +80,11 @@ def _cpu_worker(rank, world, port):
 
 def test_ep_host_logic_two_gloo_ranks():
     mp.start_processes(_cpu_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
+
+
+def test_ep_host_logic_four_gloo_ranks():
+    """Four ranks, two experts each: uneven counts per rank pair, every rank bit-exact."""
+    mp.start_processes(_cpu_worker, args=(4, _free_port()), nprocs=4, join=True, start_method="spawn")
 
 
 def test_ep_record_bytes_matches_library_formula():
