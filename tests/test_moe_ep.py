@@ -82,6 +82,42 @@ def test_ep_host_logic_two_gloo_ranks():
     mp.start_processes(_cpu_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
 
 
+def _abandon_worker(rank, world, port):
+    """Rank 1 leaves between layers (after joining the group, before the layer's first
+    exchange); rank 0's layer must end with an error from the process group -- its peer's
+    closed connection or the group's 5 s timeout -- instead of waiting for good."""
+    import datetime
+    import time
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
+    from clefq.ep import ExpertShard, omni_moe_ep
+    from tests.ep_oracle_ops import OracleEpOps
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        return
+    x, logits, gate, up, down = _cpu_problem(world)
+    per = CPU_E // world
+
+    def cut(w, rows_per_expert, cols):
+        words = cols // 8
+        return (w[0][: per * rows_per_expert * words], w[1][: per * rows_per_expert])
+    shard = ExpertShard(cut(gate, CPU_I, CPU_H), cut(up, CPU_I, CPU_H), cut(down, CPU_H, CPU_I), 0, per, CPU_E, CPU_I)
+    xt = torch.from_numpy(x[:CPU_T].view(np.int16).copy()).view(torch.bfloat16)
+    lt = torch.from_numpy(logits[:CPU_T].view(np.int16).copy()).view(torch.bfloat16)
+    t0 = time.monotonic()
+    try:
+        omni_moe_ep(xt, lt, shard, CPU_K, ops=OracleEpOps())
+    except RuntimeError:
+        assert time.monotonic() - t0 < 60
+    else:
+        raise AssertionError("the expert-parallel layer finished without its peer")
+
+
+def test_ep_departed_rank_ends_layer_with_error():
+    mp.start_processes(_abandon_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
+
+
 def test_ep_host_logic_four_gloo_ranks():
     """Four ranks, two experts each: uneven counts per rank pair, every rank bit-exact."""
     mp.start_processes(_cpu_worker, args=(4, _free_port()), nprocs=4, join=True, start_method="spawn")
