@@ -39,6 +39,7 @@ sys.path.insert(0, ROOT)
 METRIC = "INT4 MLP/MoE prefill tokens/s"
 M, HIDDEN, INTER = 4096, 4096, 12288          # C2
 MOE_T, MOE_H, MOE_I, MOE_E, MOE_K = 8192, 2048, 768, 128, 8   # C4
+C1_M, C1_K, C1_N = 128, 2048, 768                               # C1
 FLUSH_BYTES = 256 << 20
 
 
@@ -136,6 +137,16 @@ def barrier(world):
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
+
+
+def all_min(world, flag: bool) -> bool:
+    """True only if every rank's flag is true."""
+    if world == 1:
+        return bool(flag)
+    import torch.distributed as dist
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
 
 
 def all_max(world, value: float) -> float:
@@ -236,6 +247,47 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_c1(clefq, gen, flush, args, world, rank, i8_peak):
+    """project_quantized of 128 BF16 rows (K = 2048) through a 768-row
+    int4 weight -- packing of the rows plus the GEMM, timed per call with the L2 flushed in
+    between; F32 output as the config states.  Rank 0 at N = 1 also times the CPU oracle on
+    the same call."""
+    m, k, n = C1_M, C1_K, C1_N
+    w = rand_weight_dev(clefq, n, k, gen)
+    x = torch.randn(m, k, device="cuda", generator=gen).to(torch.bfloat16)
+    step = lambda: clefq.project_quantized(x, w, out_dtype=torch.float32)   # noqa: E731
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    times = time_steps(step, max(20, min(args.steps, 200)), flush, lead_cycles=400_000)
+    ms = all_max(world, statistics.median(times))
+    ops = 2.0 * m * n * k
+    out = {"workload": "C1 single INT4 GEMM: 128 x 2048 BF16 rows packed, then 768 x 2048 int4 weight, F32 out",
+           "calls": len(times), "ms_per_call": ms, "tokens_per_s": world * m / (ms / 1000),
+           "tops": ops / (ms / 1000) / 1e12, "frac_of_int8_peak": ops / (ms / 1000) / 1e12 / i8_peak,
+           "gpu_launches_per_call": 2,
+           "note": "latency-bound: 3 pair tiles on 148 SMs; the median of the per-call device times"}
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        from oracle import oracle as o
+        threads = len(os.sched_getaffinity(0))
+        rng = np.random.default_rng(0)
+        wt, ws, _ = rand_weight_host(rng, n, k)
+        xh = o.f32_to_bf16(rng.standard_normal((m, k)).astype(np.float32))
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            _, codes, scales, _ = o.prepare(xh, 4, o.stride_for(k), threads=threads)
+            o.gemm(codes, scales, wt, ws, n, k, out_f32=True, threads=threads)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= 3.0 and reps >= 5:
+                break
+        out["cpu_baseline"] = {"value": m * reps / el, "unit": "tokens/s", "cores": threads, "kind": "port",
+                               "ms_per_call": 1000 * el / reps,
+                               "sample": f"{reps} whole C1 calls ({el:.1f} s), CPU oracle port"}
+    return out
+
+
 # ---------------------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------------------
@@ -275,17 +327,18 @@ def run_clefq(args, world, rank, local):
     ms = all_max(world, ms_local)
     value = world * M / (ms / 1000)
 
-    # ---- per-kernel timing of the same step (dominant kernel: the gate|up GEMM) -------
+    # ---- per-kernel timing of the same step, each launch as clefq_mlp issues it -------
+    # The dominant kernel is the gate|up GEMM: one launch over both weight matrices
+    # (N = 2 x 12288, K = 4096, clefq_gemm_pair_s8); then the down GEMM (N = 4096, K = 12288)
+    # and the two packing passes.
     a = clefq.prepare(x, 4, clefq.stride_for(HIDDEN))
     gu = torch.zeros((M, 2 * INTER), dtype=torch.bfloat16, device="cuda")
     ktimes = {}
     reps = max(5, min(args.steps, 50))
 
     def gemm_gu():
-        clefq._call("clefq_gemm_s8", clefq._stream(), 4, clefq._ptr(a.operand), HIDDEN, clefq._ptr(a.scales), M,
-                    clefq._ptr(gate.codes), clefq._ptr(gate.scales), INTER, HIDDEN, None, 0, 0, clefq._ptr(gu),
-                    2 * INTER)
-    hid = clefq.prepare(gu[:, :INTER], 4, INTER + (128 if INTER % 1024 == 0 else 0), clefq.PREP_SWIGLU, gu[:, INTER:])
+        clefq.project_pair_prepared(M, gate, up, a, out=gu)
+    hid = clefq.prepare(gu[:, :INTER], 4, clefq.stride_for(INTER), clefq.PREP_SWIGLU, gu[:, INTER:])
     out = torch.empty((M, HIDDEN), dtype=torch.bfloat16, device="cuda")
 
     def gemm_down():
@@ -293,19 +346,21 @@ def run_clefq(args, world, rank, local):
                     clefq._ptr(down.codes), clefq._ptr(down.scales), HIDDEN, INTER, None, 0, 0, clefq._ptr(out),
                     HIDDEN)
     lead = 400_000   # ~0.2 ms of GPU spin ahead of each timed kernel
-    for name, fn in (("gemm_gate", gemm_gu), ("gemm_down", gemm_down)):
+    for name, fn in (("gemm_gate_up", gemm_gu), ("gemm_down", gemm_down)):
         fn()
         ktimes[name] = statistics.median(time_steps(fn, reps, flush, lead))
     ktimes["prepare_x"] = statistics.median(time_steps(lambda: clefq.prepare(x, 4, clefq.stride_for(HIDDEN)), reps,
                                                        flush, lead))
     ktimes["prepare_swiglu"] = statistics.median(time_steps(
-        lambda: clefq.prepare(gu[:, :INTER], 4, INTER + (128 if INTER % 1024 == 0 else 0), clefq.PREP_SWIGLU,
-                              gu[:, INTER:]), reps, flush, lead))
-    # Roofline of the down projection exactly as clefq_mlp launches it (M=4096, N=4096,
-    # K=12288): the ncu capture in profiles/ is of that launch.  Algorithmic work 2*M*N*K.
-    gemm_ops = 2.0 * M * HIDDEN * INTER
-    achieved = gemm_ops / (ktimes["gemm_down"] / 1000) / 1e12
-    traffic = load_traffic().get("gemm_c2_down", {}).get("traffic_bytes")
+        lambda: clefq.prepare(gu[:, :INTER], 4, clefq.stride_for(INTER), clefq.PREP_SWIGLU, gu[:, INTER:]), reps,
+        flush, lead))
+    # Rooflines of the two GEMM launches exactly as clefq_mlp issues them; algorithmic work
+    # 2*M*N*K each (gate|up: N = 2 x INTER, K = HIDDEN; down: N = HIDDEN, K = INTER).
+    traffic_tab = load_traffic()
+    gu_ops = 2.0 * M * (2 * INTER) * HIDDEN
+    gu_achieved = gu_ops / (ktimes["gemm_gate_up"] / 1000) / 1e12
+    down_ops = 2.0 * M * HIDDEN * INTER
+    down_achieved = down_ops / (ktimes["gemm_down"] / 1000) / 1e12
 
     # ---- end to end through the public API with host buffers ---------------------------
     # clefq.mlp_host (clefq_mlp_host): pinned host rows in, pinned host rows out, K calls back
@@ -353,23 +408,40 @@ def run_clefq(args, world, rank, local):
         mx = torch.randn(MOE_T, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
         wr = torch.randn(MOE_E, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
         logits = mx @ wr.t()     # router linear (BF16, cuBLAS): outside the INT4 path
+        # The expert weights are the same on every rank (one seed): rank r keeps its slice, and
+        # the full set gives the single-GPU result each rank's expert-parallel output must equal.
+        wgen = torch.Generator(device="cuda")
+        wgen.manual_seed(2000)
+        mg = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, wgen)
+        mu = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, wgen)
+        md = rand_weight_dev(clefq, MOE_E * MOE_H, MOE_I, wgen)
+        mws = torch.empty(clefq.lib().clefq_moe_workspace_size(MOE_T, MOE_H, MOE_I, MOE_E, MOE_K),
+                          dtype=torch.uint8, device="cuda")
         nccl_ms = None
+        parity = None
         if world > 1:
             # expert parallel: this rank owns MOE_E / world experts and its own MOE_T tokens;
             # one clefq_moe_ep_layer call per step (records and products stored into the peers'
             # symmetric buffers by the kernels), the NCCL all-to-all composition timed beside it
             from clefq.comm import Comm
-            from clefq.ep import ExpertShard, ep_layer_region_bytes, omni_moe_ep, omni_moe_ep_fused
-            per = MOE_E // world
-            shard = ExpertShard(rand_weight_dev(clefq, per * MOE_I, MOE_H, gen),
-                                rand_weight_dev(clefq, per * MOE_I, MOE_H, gen),
-                                rand_weight_dev(clefq, per * MOE_H, MOE_I, gen), rank * per, per, MOE_E, MOE_I)
+            from clefq.ep import ep_layer_region_bytes, omni_moe_ep, omni_moe_ep_fused, shard_experts
+            shard = shard_experts(mg, mu, md, MOE_E, MOE_I, MOE_H, rank, world)
             cap = world * MOE_T * MOE_K
             ecomm = Comm(ep_layer_region_bytes(MOE_T, MOE_H, MOE_K, world, cap))
             ews = torch.empty(clefq.lib().clefq_moe_ep_layer_workspace_size(MOE_T, MOE_H, MOE_I, MOE_E, MOE_K, world,
                                                                             cap), dtype=torch.uint8, device="cuda")
             eout = torch.empty((MOE_T, MOE_H), dtype=torch.bfloat16, device="cuda")
             nstep = lambda: omni_moe_ep(mx, logits, shard, MOE_K)   # noqa: E731
+            # parity before timing: both expert-parallel paths against clefq_moe on one GPU
+            ref = clefq.omni_moe(mx, logits, mg, mu, md, workspace=mws)
+            nccl_out = nstep()[0]
+            omni_moe_ep_fused(mx, logits, shard, ecomm, MOE_K, recv_cap=cap, workspace=ews, out=eout)
+            torch.cuda.synchronize()
+            clefq.status()
+            same = torch.equal(eout.view(torch.int16), ref.view(torch.int16)) and \
+                torch.equal(nccl_out.view(torch.int16), ref.view(torch.int16))
+            parity = all_min(world, same)
+            del ref, nccl_out
             for _ in range(3):
                 nstep()
             torch.cuda.synchronize()
@@ -379,11 +451,6 @@ def run_clefq(args, world, rank, local):
             mstep = lambda: omni_moe_ep_fused(mx, logits, shard, ecomm, MOE_K, recv_cap=cap,  # noqa: E731
                                               workspace=ews, out=eout)
         else:
-            mg = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
-            mu = rand_weight_dev(clefq, MOE_E * MOE_I, MOE_H, gen)
-            md = rand_weight_dev(clefq, MOE_E * MOE_H, MOE_I, gen)
-            mws = torch.empty(clefq.lib().clefq_moe_workspace_size(MOE_T, MOE_H, MOE_I, MOE_E, MOE_K),
-                              dtype=torch.uint8, device="cuda")
             mstep = lambda: clefq.omni_moe(mx, logits, mg, mu, md, workspace=mws)   # noqa: E731
         for _ in range(3):
             mstep()
@@ -396,35 +463,55 @@ def run_clefq(args, world, rank, local):
         if world > 1:
             ecomm.close()
         ops = 2.0 * MOE_T * MOE_K * (MOE_H * 2 * MOE_I + MOE_I * MOE_H)
-        moe_roof = None
         if world > 1:
             rec_b = clefq.lib().clefq_moe_ep_record_bytes(MOE_H)
             link = (world - 1) / world * MOE_T * MOE_K * (rec_b + 2 * MOE_H)   # records out, products back
             target = max(ops / (i8_peak * 1e12), link / 770e9) * 1e3
             moe_roof = {"target_ms": target, "frac": target / mms, "int_ops_per_rank": ops,
                         "nvlink_bytes_per_rank": link}
+        else:
+            # the whole layer against the int8 tensor peak (its GEMMs are 0.62 T int ops), and
+            # the dominant launch -- the grouped gate|up expert GEMM -- timed alone below
+            moe_roof = {"bound": "tensor", "kernel": "the whole clefq_moe layer (7 launches)",
+                        "achieved": ops / (mms / 1000) / 1e12, "peak": i8_peak, "unit": "TOP/s",
+                        "frac": ops / (mms / 1000) / 1e12 / i8_peak, "algorithmic_ops": ops,
+                        "traffic": traffic_tab.get("moe_c4_layer", {}).get("traffic_bytes")}
         moe = {"workload": "C4 Omni INT4 MoE layer: 8192 tokens per GPU, hidden 2048, 128 experts x (gate|up "
                            "2048->2x768, down 768->2048), top-8", "roofline": moe_roof,
                "parallelism": f"ep{world}: experts sharded; one clefq_moe_ep_layer call, dispatch and return "
                               "stored into peers' buffers over NVLink by the kernels" if world > 1
                else "single GPU", "tokens_per_s": world * MOE_T / (mms / 1000), "ms_per_step": mms,
                "nccl_all_to_all_ms_per_step": nccl_ms,
+               "parity": parity,
+               "parity_note": "each rank's fused and NCCL expert-parallel outputs equal clefq_moe over the same "
+                              "tokens with all 128 experts on one GPU, bit for bit (all ranks)" if world > 1 else
+                              "tests/test_gpu_fullsize.py checks this layer at full size against the CPU oracle",
                "tops": ops / (mms / 1000) / 1e12, "frac_of_int8_peak": ops / (mms / 1000) / 1e12 / i8_peak}
+        del mg, mu, md, mws
 
     # ---- tensor-parallel C2 block (N > 1): one 4096-token block shared by all ranks -------
     tp = None
     if world > 1 and not args.skip_tp:
-        from clefq.tp import MlpShard, TpComm, mlp_tp, mlp_tp_fused, tp_mlp_region_bytes
+        from clefq.tp import TpComm, mlp_tp, mlp_tp_fused, shard_mlp, tp_mlp_region_bytes
         tgen = torch.Generator(device="cuda")
-        tgen.manual_seed(77)                    # the same input on every rank
+        tgen.manual_seed(77)                    # the same input and weights on every rank
         tx = torch.randn(M, HIDDEN, device="cuda", generator=tgen).to(torch.bfloat16)
-        tshard = MlpShard(rand_weight_dev(clefq, INTER // world, HIDDEN, gen),
-                          rand_weight_dev(clefq, INTER // world, HIDDEN, gen),
-                          rand_weight_dev(clefq, HIDDEN // world, INTER, gen), rank, world, HIDDEN, INTER)
+        tg, tu, td = (rand_weight_dev(clefq, INTER, HIDDEN, tgen), rand_weight_dev(clefq, INTER, HIDDEN, tgen),
+                      rand_weight_dev(clefq, HIDDEN, INTER, tgen))
+        tshard = shard_mlp(tg, tu, td, rank, world)
         comm = TpComm(tp_mlp_region_bytes(M, HIDDEN, INTER, world))
         tws = torch.empty(clefq.lib().clefq_tp_mlp_workspace_size(M, HIDDEN, INTER, world), dtype=torch.uint8,
                           device="cuda")
         tout = torch.empty((M, HIDDEN), dtype=torch.bfloat16, device="cuda")
+        # parity before timing: both tensor-parallel paths against clefq_mlp on one GPU
+        tref = clefq.mlp(tx, tg, tu, td)
+        nccl_out = mlp_tp(tx, tshard)
+        mlp_tp_fused(tx, tshard, comm, workspace=tws, out=tout)
+        torch.cuda.synchronize()
+        clefq.status()
+        tp_parity = all_min(world, torch.equal(tout.view(torch.int16), tref.view(torch.int16)) and
+                            torch.equal(nccl_out.view(torch.int16), tref.view(torch.int16)))
+        del tref, nccl_out
 
         def timed(step):
             for _ in range(3):
@@ -453,7 +540,16 @@ def run_clefq(args, world, rank, local):
                              "device barriers", "scaling": "strong",
               "tokens_per_s": M / (fms / 1000), "ms_per_step": fms,
               "nccl_collectives_ms_per_step": nms,
+              "parity": tp_parity,
+              "parity_note": "every rank's fused and NCCL tensor-parallel outputs equal clefq_mlp on one GPU "
+                             "with the full weights, bit for bit",
               "gpu_launches_per_step": 8}
+        del tg, tu, td
+
+    # ---- C1: one 128 x 2048 -> 768 projection, GPU and CPU ---------
+    c1 = None
+    if not args.skip_c1:
+        c1 = run_c1(clefq, gen, flush, args, world, rank, i8_peak)
 
     launches = 4 * args.steps
     line = {
@@ -462,11 +558,19 @@ def run_clefq(args, world, rank, local):
         "dtype": "int4 x int4 -> int32 (tcgen05 kind::i8), f32 epilogue, bf16 activations",
         "data": "synthetic (seed 1000+rank): x bf16 N(0,1), codes uniform [-8,7], scales |N(0,0.02)|/7",
         "config": run_config(world),
-        "roofline": {"bound": "tensor", "kernel": "gemm_i8_2sm_kernel (C2 down GEMM M=4096 N=4096 K=12288)",
-                     "achieved": achieved, "peak": i8_peak, "unit": "TOP/s", "frac": achieved / i8_peak,
-                     "traffic": traffic,
+        "roofline": {"bound": "tensor",
+                     "kernel": "gemm_i8_2sm_kernel (C2 gate|up GEMM as clefq_mlp launches it: M=4096, "
+                               "N=2x12288 over two weight maps, K=4096)",
+                     "achieved": gu_achieved, "peak": i8_peak, "unit": "TOP/s", "frac": gu_achieved / i8_peak,
+                     "traffic": traffic_tab.get("gemm_c2_gate_up", {}).get("traffic_bytes"),
+                     "algorithmic_ops": gu_ops,
                      "peak_note": f"kind::i8 dense = 2 x {peak_kind} bf16 burst ({bf16_peak} TF/s) from "
                                   "MEASURED_PEAKS.json"},
+        "roofline_down": {"bound": "tensor", "kernel": "gemm_i8_2sm_kernel (C2 down GEMM M=4096 N=4096 K=12288)",
+                          "achieved": down_achieved, "peak": i8_peak, "unit": "TOP/s",
+                          "frac": down_achieved / i8_peak,
+                          "traffic": traffic_tab.get("gemm_c2_down", {}).get("traffic_bytes"),
+                          "algorithmic_ops": down_ops},
         "kernels_ms": ktimes,
         "e2e": {"value": world * M / (e2e_ms / 1000), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "api": "clefq.mlp_host (clefq_mlp_host), pinned host buffers, calls back to back",
@@ -475,6 +579,8 @@ def run_clefq(args, world, rank, local):
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if c1:
+        line["c1"] = c1
     if moe:
         line["secondary"] = moe
     if tp:
@@ -498,6 +604,7 @@ def main():
     ap.add_argument("--skip-moe", action="store_true")
     ap.add_argument("--skip-tp", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-c1", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0,
                     help="calls in the timed e2e stream (default: --steps clamped to [100, 200]); "
                          "small values keep profiler captures short")

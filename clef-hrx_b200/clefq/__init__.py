@@ -35,6 +35,7 @@ _SYMBOLS = {
     "clefq_gemm": (ctypes.c_int, ["p", "i", "p", "l", "p", "l", "p", "p", "l", "l", "p", "l", "i", "p", "l", "p", "l"]),
     "clefq_gemm_s8": (ctypes.c_int, ["p", "i", "p", "l", "p", "l", "p", "p", "l", "l", "p", "l", "i", "p", "l"]),
     "clefq_gemm_noalloc": (ctypes.c_int, ["p", "p", "l", "p", "l", "p", "p", "l", "l", "p", "l", "i", "p", "l"]),
+    "clefq_gemm_pair_s8": (ctypes.c_int, ["p", "p", "l", "p", "l", "p", "p", "p", "p", "l", "l", "p", "l"]),
     "clefq_swiglu": (ctypes.c_int, ["p", "p", "p", "l", "p"]),
     "clefq_route": (ctypes.c_int, ["p", "p", "i", "l", "i", "i", "p"]),
     "clefq_group_workspace_size": (ctypes.c_int64, ["l", "i", "i"]),
@@ -45,6 +46,8 @@ _SYMBOLS = {
     "clefq_combine": (ctypes.c_int, ["p", "p", "p", "p", "l", "i", "l", "p"]),
     "clefq_mlp_workspace_size": (ctypes.c_int64, ["l", "l", "l"]),
     "clefq_mlp": (ctypes.c_int, ["p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "p", "l"]),
+    "clefq_normalized_mlp": (ctypes.c_int, ["p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "p",
+                                            "l"]),
     "clefq_mlp_host_workspace_size": (ctypes.c_int64, ["l", "l", "l", "i"]),
     "clefq_mlp_host": (ctypes.c_int, ["p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "l", "i", "p",
                                       "p", "l"]),
@@ -291,6 +294,42 @@ def mlp(x, gate: QuantizedWeight, up: QuantizedWeight, down: QuantizedWeight, re
         workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
     _call("clefq_mlp", _stream(), _ptr(x), m, hidden, inter, _ptr(gate.codes), _ptr(gate.scales), _ptr(up.codes),
           _ptr(up.scales), _ptr(down.codes), _ptr(down.scales), _ptr(residual), _ptr(out), _ptr(workspace), need)
+    return out
+
+
+def normalized_mlp(x, norm_weight, gate: QuantizedWeight, up: QuantizedWeight, down: QuantizedWeight, out=None,
+                   workspace=None):
+    """Pre-norm MLP block with x as its residual (src/quantized.rs:348-404), one C-ABI call:
+    RMSNorm fused into the packing of x -> gate|up -> SwiGLU packing -> down + x.
+    norm_weight: BF16 [hidden] (applied as weight + 1, eps 1e-6).  out may be x."""
+    _need_cuda(x, norm_weight)
+    m, hidden = x.shape
+    inter = gate.rows
+    if not (gate.cols == up.cols == hidden and up.rows == inter and down.cols == inter and down.rows == hidden):
+        raise ValueError("MLP weight shapes do not chain")
+    if norm_weight.shape != (hidden,) or norm_weight.dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
+        raise ValueError("normalized MLP shape/dtype mismatch")
+    if out is None:
+        out = torch.empty((m, hidden), dtype=torch.bfloat16, device=x.device)
+    need = lib().clefq_mlp_workspace_size(m, hidden, inter)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    _call("clefq_normalized_mlp", _stream(), _ptr(x), m, hidden, inter, _ptr(norm_weight.contiguous()),
+          _ptr(gate.codes), _ptr(gate.scales), _ptr(up.codes), _ptr(up.scales), _ptr(down.codes), _ptr(down.scales),
+          _ptr(out), _ptr(workspace), need)
+    return out
+
+
+def project_pair_prepared(rows, w0: QuantizedWeight, w1: QuantizedWeight, a: Prepared, out=None):
+    """Two projections of one prepared input in one launch (gate and up of an MLP):
+    returns BF16 [rows][2n] = [x.w0 | x.w1] (clefq_gemm_pair_s8)."""
+    if a.operand is None or a.bits != 4 or w0.rows != w1.rows or w0.cols != w1.cols:
+        raise ValueError("paired projection needs an int4 s8 operand and two weights of one shape")
+    n = w0.rows
+    if out is None:
+        out = torch.empty((rows, 2 * n), dtype=torch.bfloat16, device=a.codes.device)
+    _call("clefq_gemm_pair_s8", _stream(), _ptr(a.operand), a.operand.stride(0), _ptr(a.scales), rows,
+          _ptr(w0.codes), _ptr(w0.scales), _ptr(w1.codes), _ptr(w1.scales), n, w0.cols, _ptr(out), out.stride(0))
     return out
 
 

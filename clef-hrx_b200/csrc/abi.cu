@@ -44,6 +44,7 @@ static __device__ int g_status_word;
 
 namespace {
 thread_local char g_err[512] = "";
+thread_local cudaError_t g_launch_err = cudaSuccess;
 std::mutex g_mu;
 int g_sms[64];
 int *g_status_ptr[64];
@@ -57,6 +58,7 @@ int set_err(int code, const char *fmt, ...) {
 }
 int cuda_err(const char *what) {
   cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = g_launch_err;  // a launch helper already took it
   return set_err(CLEFQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 int current_device() {
@@ -70,6 +72,14 @@ bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
 // Records a failure message for clefq_last_error() from another translation unit.
 int report_error(int code, const char *msg) { return set_err(code, "%s", msg); }
+
+int launch_check() {
+  const cudaError_t e = cudaGetLastError();
+  g_launch_err = e;
+  return e == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+}
+
+cudaError_t last_launch_error() { return g_launch_err; }
 
 int device_sms() {
   const int d = current_device();
@@ -307,6 +317,18 @@ int clefq_gemm_s8(void *stream, int bits, const void *operand, int64_t operand_l
                   out_dtype, out, out_ld);
 }
 
+int clefq_gemm_pair_s8(void *stream, const void *operand, int64_t operand_ld, const float *a_scales, int64_t m,
+                       const void *w0_tiled, const float *w0_scales, const void *w1_tiled, const float *w1_scales,
+                       int64_t n, int64_t k, void *out, int64_t out_ld) {
+  int rc = check_gemm(4, m, 2 * n, k, operand_ld, nullptr, 0, CLEFQ_BF16, out_ld);
+  if (rc) return rc;
+  if (!w0_tiled || !w1_tiled) return set_err(CLEFQ_ERR_SHAPE, "two weight matrices needed");
+  if (m == 0) return 0;
+  return run_gemm(static_cast<cudaStream_t>(stream), 4, static_cast<const uint8_t *>(operand), operand_ld, m, a_scales,
+                  m, w0_tiled, w0_scales, w1_tiled, w1_scales, (int)(n / 128), 2 * n, k, nullptr, 0, CLEFQ_BF16, out,
+                  out_ld);
+}
+
 int clefq_swiglu(void *stream, const void *gate, const void *up, int64_t n, void *out) {
   if (n < 0) return set_err(CLEFQ_ERR_SHAPE, "SwiGLU shape/dtype mismatch");
   if (n == 0) return 0;
@@ -463,12 +485,15 @@ int64_t clefq_mlp_workspace_size(int64_t m, int64_t hidden, int64_t inter) {
   return aligned_total(a);
 }
 
-int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t inter, const void *gate_tiled,
-              const float *gate_scales, const void *up_tiled, const float *up_scales, const void *down_tiled,
-              const float *down_scales, const void *residual, void *out, void *workspace, int64_t workspace_bytes) {
+// The MLP block behind clefq_mlp and clefq_normalized_mlp: norm_weight == NULL packs x as it
+// is; otherwise x is RMS-normalised with that weight inside its packing (the reference's
+// prepare_norm_with_source) and the un-normalised x is the down projection's residual.
+static int run_mlp(cudaStream_t s, const void *x, int64_t m, int64_t hidden, int64_t inter, const void *norm_weight,
+                   const void *gate_tiled, const float *gate_scales, const void *up_tiled, const float *up_scales,
+                   const void *down_tiled, const float *down_scales, const void *residual, void *out, void *workspace,
+                   int64_t workspace_bytes) {
   if (m < 1 || hidden % 256 || inter % 256 || hidden < 256 || inter < 256 || hidden > 32768 || inter > 32768)
     return set_err(CLEFQ_ERR_SHAPE, "unsupported MLP shape");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint32_t *xq, *hq;
   uint8_t *x8, *h8;
   uint16_t *gu;
@@ -476,7 +501,10 @@ int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t in
                        &h8);
   if (!a.ok || !workspace) return set_err(CLEFQ_ERR_WORKSPACE, "mlp workspace too small");
   const int64_t sh = stride_for(hidden), si = stride_for(inter);
-  int rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, m, hidden, sh, xq, x8, hidden, nullptr, 0);
+  int rc = norm_weight ? run_prepare(s, CLEFQ_PREP_NORM, 4, x, hidden, norm_weight, 0, m, hidden, sh, xq, x8, hidden,
+                                     nullptr, 0)
+                       : run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, m, hidden, sh, xq, x8, hidden,
+                                     nullptr, 0);
   if (rc) return rc;
   // gate and up in one launch: output columns [0, inter) gate, [inter, 2*inter) up
   rc = run_gemm(s, 4, x8, hidden, m, reinterpret_cast<const float *>(xq + m * (sh / 8)), m, gate_tiled, gate_scales,
@@ -487,6 +515,22 @@ int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t in
   if (rc) return rc;
   return run_gemm(s, 4, h8, inter, m, reinterpret_cast<const float *>(hq + m * (si / 8)), m, down_tiled, down_scales,
                   nullptr, nullptr, (int)(hidden / 128), hidden, inter, residual, hidden, CLEFQ_BF16, out, hidden);
+}
+
+int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t inter, const void *gate_tiled,
+              const float *gate_scales, const void *up_tiled, const float *up_scales, const void *down_tiled,
+              const float *down_scales, const void *residual, void *out, void *workspace, int64_t workspace_bytes) {
+  return run_mlp(static_cast<cudaStream_t>(stream), x, m, hidden, inter, nullptr, gate_tiled, gate_scales, up_tiled,
+                 up_scales, down_tiled, down_scales, residual, out, workspace, workspace_bytes);
+}
+
+int clefq_normalized_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t inter,
+                         const void *norm_weight, const void *gate_tiled, const float *gate_scales,
+                         const void *up_tiled, const float *up_scales, const void *down_tiled,
+                         const float *down_scales, void *out, void *workspace, int64_t workspace_bytes) {
+  if (!norm_weight) return set_err(CLEFQ_ERR_SHAPE, "normalized MLP needs the RMSNorm weight");
+  return run_mlp(static_cast<cudaStream_t>(stream), x, m, hidden, inter, norm_weight, gate_tiled, gate_scales,
+                 up_tiled, up_scales, down_tiled, down_scales, x, out, workspace, workspace_bytes);
 }
 
 // ---- tensor-parallel MLP block, collectives fused into its kernels --------------------

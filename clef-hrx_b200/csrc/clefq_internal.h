@@ -203,6 +203,10 @@ int launch_ep_receive(const EpReceiveArgs &a, cudaStream_t stream, int num_sms);
 
 int device_sms();
 int report_error(int code, const char *msg);  // sets clefq_last_error()
+// After a kernel launch: 0, or CLEFQ_ERR_CUDA with CUDA's error kept for this thread, so
+// the caller's message (last_launch_error) can name it although the error state is cleared.
+int launch_check();
+cudaError_t last_launch_error();
 int *device_status_word();  // per-device zero-initialised status word used by bounded waits
 
 }  // namespace cq

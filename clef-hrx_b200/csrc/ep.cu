@@ -71,7 +71,7 @@ int launch_ep_pack(const uint32_t *xq, int64_t words_ld, const float *scales, co
   int64_t blocks = (total + 7) / 8, cap = (int64_t)num_sms * 16;
   ep_pack_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(xq, words_ld, scales, routes, slots,
                                                                               tokens, topk, code_words, rec_words, send);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // Received records -> contiguous activation scales and one-route-per-record routes
@@ -95,7 +95,7 @@ int launch_ep_unpack_meta(const uint32_t *recv, int64_t n, int code_words, int64
   int64_t blocks = (n + 255) / 256, cap = (int64_t)num_sms * 8;
   ep_unpack_meta_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(
       recv, n, code_words, rec_words, expert_base, local_experts, scales, routes);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // products[i] = bf16(bf16(values[i]) * probability of record i): the per-route term of the
@@ -124,7 +124,7 @@ int launch_ep_weigh(const uint16_t *values, const float *routes, int64_t n, int6
   if (total == 0) return 0;
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   ep_weigh_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(values, routes, n, width, products);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // Home rank: out[t] = the ascending-expert chain s = bf16(s + product) over the token's
@@ -174,7 +174,7 @@ int launch_ep_combine(const uint16_t *products, const int *slots, const float *r
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   ep_combine_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(products, slots, routes, tokens, topk,
                                                                                  width, out);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 
@@ -260,14 +260,14 @@ int launch_ep_dispatch(const EpDispatchArgs &a, cudaStream_t stream, int num_sms
   if (total == 0) return 0;
   int64_t blocks = (total + 7) / 8, cap = (int64_t)num_sms * 16;
   ep_dispatch_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 int launch_ep_receive(const EpReceiveArgs &a, cudaStream_t stream, int num_sms) {
   int64_t blocks = (a.recv_cap + 255) / 256, cap = (int64_t)num_sms * 8;
   if (blocks < 1) blocks = 1;
   ep_receive_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 }  // namespace cq

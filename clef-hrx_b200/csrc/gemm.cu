@@ -556,7 +556,7 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
     if (p.bits == 4) launch_variant<false, 4>(grid, tmap, wmap0, wmap1, p, stream);
     else launch_variant<false, 8>(grid, tmap, wmap0, wmap1, p, stream);
   }
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 }  // namespace cq

@@ -33,7 +33,7 @@ int launch_untile(const uint16_t *src, int64_t rows, int64_t cols, uint16_t *dst
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   untile_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(
       reinterpret_cast<const uint4 *>(src), rows, cols, reinterpret_cast<uint4 *>(dst));
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 namespace {

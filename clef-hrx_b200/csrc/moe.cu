@@ -78,7 +78,7 @@ int launch_route(const void *logits, int is_f32, int64_t tokens, int experts, in
   const int warps = 8;
   route_kernel<<<(unsigned)((tokens + warps - 1) / warps), warps * 32, 0, stream>>>(logits, is_f32, tokens, experts,
                                                                                      topk, routes);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // ---- stable grouping: a three-phase counting sort of route items by key ----------------
@@ -311,7 +311,7 @@ int launch_sort(SortArgs a, cudaStream_t stream) {
   sort_scan_kernel<<<1, 512, 0, stream>>>(a, chunks);
   if (chunks > 0)
     sort_scatter_kernel<<<chunks, 256, sizeof(int) * 8 * a.keys, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 int launch_group(const float *routes, int64_t tokens, int topk, int experts, int tile_rows, int *counts, int *offsets,
@@ -366,7 +366,7 @@ __global__ void tasks_kernel(const float *__restrict__ groups, int64_t tokens, i
 int launch_tasks(const float *groups, int64_t tokens, int experts, float *tasks, cudaStream_t stream) {
   if (experts > 1024) return CLEFQ_ERR_SHAPE;
   tasks_kernel<<<1, ((experts + 31) / 32) * 32, 0, stream>>>(groups, tokens, experts, tasks);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // Sorted-layout tables from a reference-format groups buffer: offsets, perm, tile list.
@@ -417,7 +417,7 @@ int launch_groups_to_sorted(const float *groups, int64_t tokens, int topk, int e
                             int *perm, int *tile_list, cudaStream_t stream) {
   if (experts > 1024) return CLEFQ_ERR_SHAPE;
   groups_to_sorted_kernel<<<1, 256, 0, stream>>>(groups, tokens, topk, experts, tile_rows, offsets, perm, tile_list);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // dst[p][:] = src[row(p)][:], row(p) = perm[p] / div (16-byte vectors).
@@ -440,7 +440,7 @@ int launch_gather(const uint8_t *src, int64_t src_ld, const int *perm, int div, 
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   gather_rows_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(src, src_ld, perm, div, rows,
                                                                                   row_bytes, dst, dst_ld);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // Weighted combine in ascending expert order with BF16 rounding at every step; eight
@@ -605,7 +605,7 @@ int launch_combine(const uint16_t *values, const float *routes, const float *ord
     const unsigned g16 = (unsigned)(b16 < cap16 ? b16 : cap16);
     if (weighted) combine_k_kernel<8, true, 16><<<g16, 128, 0, stream>>>(values, routes, order, tokens, width, out);
     else combine_k_kernel<8, false, 16><<<g16, 128, 0, stream>>>(values, routes, order, tokens, width, out);
-    return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+    return launch_check();
   }
 #define CQ_COMBINE_K(K)                                                                            \
   (weighted ? combine_k_kernel<K, true, 8><<<grid, 256, 0, stream>>>(values, routes, order, tokens, width, out) \
@@ -617,7 +617,7 @@ int launch_combine(const uint16_t *values, const float *routes, const float *ord
     default: combine_kernel<<<grid, 256, 0, stream>>>(values, routes, order, tokens, topk, width, out, weighted); break;
   }
 #undef CQ_COMBINE_K
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 
@@ -656,7 +656,7 @@ int launch_gather_unpack_i4(const uint32_t *a, int64_t a_ld, const int *perm, in
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   gather_unpack_i4_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(a, a_ld, perm, div, rows,
                                                                                        rows_dev, k, dst, dst_ld);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 }  // namespace cq

@@ -8,14 +8,21 @@
 // array that is part of this library's device image instead.
 //
 // Costs and limits of the fixed scratch:
-//   * every GPU on which this entry point has been used holds NOALLOC_SCRATCH_BYTES of
-//     device memory for the rest of the process (the array lives in this file's module,
-//     which the CUDA runtime loads on first use);
+//   * the array lives in this library's device module.  With the CUDA runtime's default
+//     lazy module loading (CUDA 12.2 and later) the module, and with it the 64 MiB, is
+//     loaded on a device the first time this entry point runs there, and stays until the
+//     process exits.  With CUDA_MODULE_LOADING=EAGER every device on which the library
+//     creates a context holds the 64 MiB, whether or not it ever calls this;
 //   * one array per device is shared by all calls: calls whose kernels overlap on the GPU
 //     (other streams, other host threads) race on it and must be serialised by the caller;
 //   * m * k must not exceed NOALLOC_SCRATCH_BYTES; larger problems get CLEFQ_ERR_WORKSPACE.
 // The first call on each device looks up the array's device address with the device
-// current; nothing here calls cudaMalloc, cudaFree or any allocating routine.
+// current; that lookup is what loads the module.  A call with m == 0 does the lookup and
+// nothing else, so a host whose allocator will take all of device memory makes one such
+// call on each device before reserving it.  Nothing here calls cudaMalloc, cudaFree or any
+// allocating routine.
+#include <stdio.h>
+
 #include <mutex>
 
 #include "clefq_internal.h"
@@ -31,6 +38,14 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES
 
 namespace {
 std::mutex g_noalloc_mu;
+
+// Records "clefq_gemm_noalloc: <what>: <CUDA's message>" for clefq_last_error().
+int cuda_failure(const char *what, cudaError_t e) {
+  char msg[256];
+  snprintf(msg, sizeof msg, "clefq_gemm_noalloc: %s: %s", what, cudaGetErrorString(e));
+  return report_error(CLEFQ_ERR_CUDA, msg);
+}
+
 uint8_t *g_noalloc_ptr[64];
 
 // Device address of this device's scratch array (looked up once per device).
@@ -44,7 +59,7 @@ int scratch_for_current_device(uint8_t **out) {
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p) {
       cudaGetLastError();
-      return report_error(CLEFQ_ERR_CUDA, "clefq_gemm_noalloc: cannot resolve the scratch array on this device");
+      return cuda_failure("cannot resolve the scratch array on this device", e);
     }
     g_noalloc_ptr[dev] = static_cast<uint8_t *>(p);
   }
@@ -68,15 +83,17 @@ extern "C" __attribute__((visibility("default"))) int clefq_gemm_noalloc(
   if (m * k > NOALLOC_SCRATCH_BYTES)
     return report_error(CLEFQ_ERR_WORKSPACE,
                         "clefq_gemm_noalloc: m * k exceeds the 64 MiB built-in scratch; use clefq_gemm with a workspace");
-  if (m == 0) return 0;
+  // Resolve the scratch first, also for m == 0: that call is the documented way to load
+  // the array on a device before the host's allocator takes the rest of its memory.
   uint8_t *op = nullptr;
   int rc = scratch_for_current_device(&op);
   if (rc) return rc;
+  if (m == 0) return 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // The unpack kernel rewrites every byte of [m][k] that the GEMM reads; nothing needs
   // clearing between calls.
   rc = launch_unpack_i4(static_cast<const uint32_t *>(a_codes), a_ld_words, m, (int)k, op, k, s, device_sms());
-  if (rc) return report_error(CLEFQ_ERR_CUDA, "clefq_gemm_noalloc: unpack launch failed");
+  if (rc) return cuda_failure("unpack launch failed", last_launch_error());
   int *status = device_status_word();
   if (!status) return report_error(CLEFQ_ERR_CUDA, "clefq_gemm_noalloc: status word");
   GemmParams p{};
@@ -98,7 +115,7 @@ extern "C" __attribute__((visibility("default"))) int clefq_gemm_noalloc(
   p.ldr = residual_ld;
   p.err = status;
   rc = launch_gemm(p, s);
-  if (rc == CLEFQ_ERR_CUDA) return report_error(rc, "clefq_gemm_noalloc: gemm launch failed");
+  if (rc == CLEFQ_ERR_CUDA) return cuda_failure("gemm launch failed", last_launch_error());
   if (rc) return report_error(rc, "clefq_gemm_noalloc: unsupported shape or alignment");
   return 0;
 }

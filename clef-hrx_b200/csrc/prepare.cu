@@ -881,7 +881,7 @@ int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n
     int64_t rest = n - done;
     swiglu_tail_kernel<<<(unsigned)((rest + 255) / 256), 256, 0, stream>>>(g, u, out, done, n);
   }
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -914,7 +914,7 @@ int launch_retile(const uint32_t *codes, int64_t rows, int64_t in_words, int64_t
   if (total4 == 0) return 0;
   int64_t blocks = (total4 + 255) / 256, cap = (int64_t)num_sms * 16;
   retile_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(codes, in_words, words, rows, out);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -950,7 +950,7 @@ int launch_unpack_i4(const uint32_t *a, int64_t a_ld, int64_t rows, int k, uint8
   if (total == 0) return 0;
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   unpack_i4_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(a, a_ld, rows, k, op, op_ld);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 }  // namespace cq

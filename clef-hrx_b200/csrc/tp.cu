@@ -42,7 +42,7 @@ int launch_tp_gather_unpack(const uint32_t *codes, int world, int64_t rows, int 
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   tp_gather_unpack_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(codes, world, rows,
                                                                                        shard_words, op, op_ld);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 // src [G][rows][shard_bytes] -> dst [rows][dst_ld]: dst[m][g*shard_bytes + j] = src[g][m][j],
@@ -68,7 +68,7 @@ int launch_tp_interleave(const uint8_t *src, int world, int64_t rows, int64_t sh
   int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms * 16;
   tp_interleave_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(src, world, rows, shard_bytes, dst,
                                                                                     dst_ld);
-  return cudaGetLastError() == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+  return launch_check();
 }
 
 }  // namespace cq

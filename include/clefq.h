@@ -129,10 +129,16 @@ CLEFQ_API int clefq_gemm(void *stream, int bits, const void *a_codes, int64_t a_
  * counterpart in the reference (whose engine owns every allocation).
  * The s8 operand scratch is a fixed 64 MiB array inside this library's device image:
  *   - m * k must be <= CLEFQ_GEMM_NOALLOC_MAX_BYTES, else CLEFQ_ERR_WORKSPACE;
- *   - every GPU on which it has been used keeps those 64 MiB until the process exits;
+ *   - with the CUDA runtime's default lazy module loading (CUDA 12.2 and later) the
+ *     64 MiB are taken on a device by the first call there and kept until the process
+ *     exits; with CUDA_MODULE_LOADING=EAGER every device on which this library has a
+ *     context holds them, whether or not it calls this function;
+ *   - the first call on a device resolves the array's address with that device current,
+ *     which is what loads it.  A call with m == 0 does only that: a host whose allocator
+ *     reserves all device memory makes one m == 0 call on each device first, otherwise
+ *     the first real call may fail with CLEFQ_ERR_CUDA (out of memory);
  *   - all calls on a device share the array, so calls that overlap on the GPU (other
- *     streams or host threads) race on it -- the caller must serialise them;
- *   - the first call on a device resolves the array's address with that device current.
+ *     streams or host threads) race on it -- the caller must serialise them.
  * Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
  */
 #define CLEFQ_GEMM_NOALLOC_MAX_BYTES (64ll << 20)
@@ -144,6 +150,17 @@ CLEFQ_API int clefq_gemm_noalloc(void *stream, const void *a_codes, int64_t a_ld
 CLEFQ_API int clefq_gemm_s8(void *stream, int bits, const void *operand, int64_t operand_ld, const float *a_scales,
                             int64_t m, const void *w_tiled, const float *w_scales, int64_t n, int64_t k,
                             const void *residual, int64_t residual_ld, int out_dtype, void *out, int64_t out_ld);
+
+/*
+ * Two projections of one prepared input in one launch, the way a SwiGLU MLP's gate and up
+ * projections share their packed activation (src/backbone.rs:880-894 calls project(gate) and
+ * project(up) on one input; src/quantized.rs:254-280 reuses its packed codes):
+ *   out[:, 0:n] = projection by w0, out[:, n:2n] = projection by w1, BF16 (as clefq_gemm_s8).
+ * Checks: n % 128 == 0, k % 256 == 0, out_ld >= 2n.
+ */
+CLEFQ_API int clefq_gemm_pair_s8(void *stream, const void *operand, int64_t operand_ld, const float *a_scales,
+                                 int64_t m, const void *w0_tiled, const float *w0_scales, const void *w1_tiled,
+                                 const float *w1_scales, int64_t n, int64_t k, void *out, int64_t out_ld);
 
 /* SwiGLU bf16(bf16(g/(1+exp(-g))) * u); replaces Engine::swiglu (src/ops.rs:9-29,
  * kernels/swiglu.loom:41-50).  n elements, BF16. */
@@ -213,6 +230,21 @@ CLEFQ_API int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, 
                         const float *gate_scales, const void *up_tiled, const float *up_scales, const void *down_tiled,
                         const float *down_scales, const void *residual, void *out, void *workspace,
                         int64_t workspace_bytes);
+/*
+ * Pre-norm MLP block with the input as residual; replaces normalized_mlp
+ * (src/quantized.rs:348-404): RMSNorm (weight + 1 offset, eps 1e-6, mean over `hidden`)
+ * fused into the packing of x (prepare_norm_with_source, src/quantized.rs:615-640), gate and
+ * up projections of the shared codes, SwiGLU fused into the packing of the hidden rows, and
+ * the down projection with x itself as residual:
+ *   out = bf16(x + bf16(down(swiglu(gate(norm(x)), up(norm(x))))))
+ * norm_weight BF16 [hidden].  out may be x (each element is read before it is overwritten).
+ * The reference takes this path only at width 5120 and 17408 intermediate rows; any width
+ * that is a multiple of 256 works here.  workspace >= clefq_mlp_workspace_size(m, hidden, inter).
+ */
+CLEFQ_API int clefq_normalized_mlp(void *stream, const void *x, int64_t m, int64_t hidden, int64_t inter,
+                                   const void *norm_weight, const void *gate_tiled, const float *gate_scales,
+                                   const void *up_tiled, const float *up_scales, const void *down_tiled,
+                                   const float *down_scales, void *out, void *workspace, int64_t workspace_bytes);
 /*
  * clefq_mlp from host memory to host memory: x, residual (nullable) and out are host
  * buffers [m][hidden] (pinned for the copies to overlap).  The rows run in chunks of

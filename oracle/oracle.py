@@ -225,6 +225,19 @@ def mlp_block(x, gate, up, down, threads=None):
     return gemm(hc, hs, down[0], down[1], down[2], inter, threads=threads)
 
 
+def normalized_mlp_block(x, norm_w, gate, up, down, threads=None):
+    """Pre-norm MLP with the input as residual (src/quantized.rs:348-404): RMSNorm fused into
+    the packing of x (prepare_norm_with_source), gate, up, SwiGLU, packing, down + x."""
+    m, h = x.shape
+    _, codes, scales, _ = prepare(x, 4, stride_for(h), NORM, norm_w, threads=threads)
+    g = gemm(codes, scales, gate[0], gate[1], gate[2], h, threads=threads)
+    u = gemm(codes, scales, up[0], up[1], up[2], h, threads=threads)
+    hid = swiglu(g, u, threads=threads)
+    inter = hid.shape[1]
+    _, hc, hs, _ = prepare(hid, 4, stride_for(inter), threads=threads)
+    return gemm(hc, hs, down[0], down[1], down[2], inter, residual=x, threads=threads)
+
+
 def moe_layer(x, logits, gate, up, down, topk=8, experts=128, threads=None):
     """Omni INT4 MoE block (src/omni.rs:761-857 with fast defaults): route -> ordered groups
     -> gate, up experts (shared packing) -> SwiGLU -> down experts -> ordered combine."""

@@ -167,10 +167,11 @@ def _nccl_worker(rank, world, port):
 
 
 @pytest.mark.gpu
-def test_tp_two_ranks_nccl():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    mp.start_processes(_nccl_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_ranks_nccl(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_nccl_worker, args=(world, _free_port()), nprocs=world, join=True, start_method="spawn")
 
 
 # ---------------------------------------------------------------------------------------
@@ -264,7 +265,7 @@ def _nccl_fused_worker(rank, world, port):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_fused_ranks_nccl(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
