@@ -28,6 +28,12 @@
 #include "clefq_internal.h"
 #include "cq_common.cuh"
 
+// 1: int4 pair launches take the deep-ring kernel (gemm2sm_deep.cuh); 0: the two-stage
+// kernel of gemm2sm.cuh, kept for int8 and for comparison builds.
+#ifndef CLEFQ_GEMM_DEEP
+#define CLEFQ_GEMM_DEEP 1
+#endif
+
 namespace cq {
 
 namespace {
@@ -357,6 +363,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 #include "gemm2sm.cuh"
+#include "gemm2sm_deep.cuh"
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -417,11 +424,14 @@ static void launch_variant(dim3 grid, const CUtensorMap &t, const CUtensorMap &w
   gemm_i8_kernel<G, B><<<grid, THREADS, Cfg<B>::SMEM, stream>>>(t, w0, w1, p);
 }
 
-// Launch the pair kernel on as many co-resident clusters of 2 as the device holds.
-template <bool G, int B, int SUB = 1>
-static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, const CUtensorMap &w0,
-                                      const CUtensorMap &w1, const GemmParams &p, cudaStream_t stream) {
-  using namespace two_sm;
+using PairKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmParams);
+
+// Launch a pair kernel on as many co-resident clusters of 2 as the device holds.  KEY
+// distinguishes the kernels' per-device caches.
+template <int KEY>
+static cudaError_t launch_pair_kernel(PairKernel kern, int threads, int smem, int64_t pair_tiles,
+                                      const CUtensorMap &t, const CUtensorMap &w0, const CUtensorMap &w1,
+                                      const GemmParams &p, cudaStream_t stream) {
   // per device, like the shared-memory attribute; set (release) only after the attribute call
   static std::atomic<int> max_clusters_dev[64];
   int dev = 0;
@@ -429,20 +439,19 @@ static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, 
   std::atomic<int> scratch{0};
   std::atomic<int> &slot = (dev >= 0 && dev < 64) ? max_clusters_dev[dev] : scratch;
   int max_clusters = slot.load(std::memory_order_acquire);
-  auto kern = gemm_i8_2sm_kernel<G, B, SUB>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(THREADS2);
-  cfg.dynamicSmemBytes = Cfg2<B, SUB>::SMEM;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (!max_clusters) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg2<B, SUB>::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(2 * 74);
     int n = 0;
@@ -453,6 +462,22 @@ static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, 
   const int64_t clusters = pair_tiles < max_clusters ? pair_tiles : max_clusters;
   cfg.gridDim = dim3((unsigned)(2 * clusters));
   return cudaLaunchKernelEx(&cfg, kern, t, w0, w1, p);
+}
+
+template <bool G, int B, int SUB = 1>
+static cudaError_t launch_variant_2sm(int64_t pair_tiles, const CUtensorMap &t, const CUtensorMap &w0,
+                                      const CUtensorMap &w1, const GemmParams &p, cudaStream_t stream) {
+  return launch_pair_kernel<(G ? 1 : 0) + 2 * B + 100 * SUB>(two_sm::gemm_i8_2sm_kernel<G, B, SUB>, two_sm::THREADS2,
+                                                             two_sm::Cfg2<B, SUB>::SMEM, pair_tiles, t, w0, w1, p,
+                                                             stream);
+}
+
+template <bool G, int BN>
+static cudaError_t launch_deep_2sm(int64_t pair_tiles, const CUtensorMap &t, const CUtensorMap &w0,
+                                   const CUtensorMap &w1, const GemmParams &p, cudaStream_t stream) {
+  using C = two_sm_deep::DeepCfg<BN>;
+  return launch_pair_kernel<1000 + BN + (G ? 1 : 0)>(two_sm_deep::gemm_i4_2sm_deep_kernel<G, BN>, C::THREADS, C::SMEM,
+                                                     pair_tiles, t, w0, w1, p, stream);
 }
 
 bool gemm_uses_pairs(const GemmParams &p) { return p.n_split % 2 == 0 && p.n % 256 == 0; }
@@ -511,10 +536,21 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
     wmap1 = wmap0;
   }
   if (pairs) {
+#if CLEFQ_GEMM_DEEP
+    // int4 with at least 8 K stages: the deep-ring kernel, 256-token tiles for dense launches
+    // and 192 for grouped ones (their tile lists are built for 192 rows).  Shorter K keeps
+    // the two-stage kernel, whose double-buffered accumulators hide the tile hand-over that
+    // a few K stages cannot amortise.
+    const bool deep = p.bits == 4 && p.k / 256 >= 8;
+#else
+    const bool deep = false;
+#endif
+    const int deep_bn = p.grouped ? 192 : 256;
+    const int half = deep ? deep_bn / 2 : two_sm::HALF;
     // token operand as 3D: x = 128 bytes of a K slice, y = rows (pitch a_ld), z = K slices
     cuuint64_t d3[3] = {128, (cuuint64_t)p.a_rows, (cuuint64_t)(p.k / 128)};
     cuuint64_t s3[2] = {(cuuint64_t)p.a_ld, 128};
-    cuuint32_t b3[3] = {128, (cuuint32_t)two_sm::HALF, 2};
+    cuuint32_t b3[3] = {128, (cuuint32_t)half, 2};
     cuuint32_t e3[3] = {1, 1, 1};
     if (enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(p.a_op), d3, s3, b3, e3,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -529,6 +565,15 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
     }
     const int64_t pair_tiles = tiles_m * (p.n / two_sm::BMP);
     cudaError_t e;
+    if (deep) {
+      if (p.grouped) {
+        e = launch_deep_2sm<true, 192>(pair_tiles, tmap, wmap0, wmap1, p, stream);
+      } else {
+        const int64_t tiles256 = ((p.m + 255) / 256) * (p.n / two_sm::BMP);
+        e = launch_deep_2sm<false, 256>(tiles256, tmap, wmap0, wmap1, p, stream);
+      }
+      return e == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+    }
     // dense int4 with at least two token tiles: two sub-tiles per pair tile sharing each
     // converted weight stage
     if (!p.grouped && p.bits == 4 && p.m >= 2 * two_sm::BN2) {
