@@ -559,14 +559,15 @@ def run_clefq(args, world, rank, local):
         "data": "synthetic (seed 1000+rank): x bf16 N(0,1), codes uniform [-8,7], scales |N(0,0.02)|/7",
         "config": run_config(world),
         "roofline": {"bound": "tensor",
-                     "kernel": "gemm_i8_2sm_kernel (C2 gate|up GEMM as clefq_mlp launches it: M=4096, "
-                               "N=2x12288 over two weight maps, K=4096)",
+                     "kernel": "gemm_i4_2sm_deep_kernel<dense, 256> (C2 gate|up GEMM as clefq_mlp launches it: "
+                               "M=4096, N=2x12288 over two weight maps, K=4096)",
                      "achieved": gu_achieved, "peak": i8_peak, "unit": "TOP/s", "frac": gu_achieved / i8_peak,
                      "traffic": traffic_tab.get("gemm_c2_gate_up", {}).get("traffic_bytes"),
                      "algorithmic_ops": gu_ops,
                      "peak_note": f"kind::i8 dense = 2 x {peak_kind} bf16 burst ({bf16_peak} TF/s) from "
                                   "MEASURED_PEAKS.json"},
-        "roofline_down": {"bound": "tensor", "kernel": "gemm_i8_2sm_kernel (C2 down GEMM M=4096 N=4096 K=12288)",
+        "roofline_down": {"bound": "tensor",
+                          "kernel": "gemm_i4_2sm_deep_kernel<dense, 256> (C2 down GEMM M=4096 N=4096 K=12288)",
                           "achieved": down_achieved, "peak": i8_peak, "unit": "TOP/s",
                           "frac": down_achieved / i8_peak,
                           "traffic": traffic_tab.get("gemm_c2_down", {}).get("traffic_bytes"),
