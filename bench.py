@@ -14,7 +14,10 @@ replicated weights (data-parallel replicas, no collective on the data path): wea
 The `secondary` line runs the C4 MoE layer expert-parallel (clefq_moe_ep_layer, dispatch and
 return stored into peers' buffers by the kernels; the NCCL all-to-all composition timed
 beside it) and the `tensor_parallel` line one C2 block split over the ranks (clefq_tp_mlp).
-`e2e` streams host rows through clefq.mlp_host, copies included.
+`e2e` streams host rows through clefq.mlp_host, copies included.  Further lines: `c1` (BASELINE
+configs[0], one 128 x 2048 -> 768 projection, GPU and CPU), `c3` (configs[2], the 28-layer INT4
+decoder prefill at 2048 tokens, attention glue timed apart) and `c5` (configs[4], 48 MoE layers
+at 8192 tokens per GPU, expert-parallel when N > 1).
 --impl reference: the reference's CPU semantics (the C/OpenMP oracle port; the reference
 itself is Rust + hrx-rs on an AMD gfx1151 and cannot run here) on the host cores, rank 0.
 """
@@ -40,6 +43,8 @@ METRIC = "INT4 MLP/MoE prefill tokens/s"
 M, HIDDEN, INTER = 4096, 4096, 12288          # C2
 MOE_T, MOE_H, MOE_I, MOE_E, MOE_K = 8192, 2048, 768, 128, 8   # C4
 C1_M, C1_K, C1_N = 128, 2048, 768                               # C1
+C3_S, C3_H, C3_I, C3_L, C3_QH, C3_KVH, C3_HD = 2048, 2560, 9728, 28, 32, 8, 128   # C3
+C5_L = 48                                                       # C5: 48 x the C4 MoE layer
 FLUSH_BYTES = 256 << 20
 
 
@@ -285,6 +290,191 @@ def run_c1(clefq, gen, flush, args, world, rank, i8_peak):
         out["cpu_baseline"] = {"value": m * reps / el, "unit": "tokens/s", "cores": threads, "kind": "port",
                                "ms_per_call": 1000 * el / reps,
                                "sample": f"{reps} whole C1 calls ({el:.1f} s), CPU oracle port"}
+    return out
+
+
+def run_c3(clefq, gen, flush, args, world, rank, i8_peak):
+    """a 28-layer decoder prefill, 2048 tokens, hidden 2560, 32 query / 8
+    KV heads of 128, MLP 9728, every projection INT4.  Per layer (the reference's backbone
+    call sites, src/backbone.rs:866-907): RMSNorm fused into the packing of the residual
+    stream -> one q|k|v projection (the three weights stacked by rows) -> causal GQA SDPA
+    (BF16, torch: attention is not on the INT4 path) -> o projection with the residual fused
+    -> normalized_mlp (RMSNorm packing, gate|up, SwiGLU packing, down + residual).  Rotary
+    embeddings are left out (glue outside the INT4 path).  Every rank runs its own sequence
+    (replicas).  The int4 time is the step minus the attention glue, both CUDA-event timed."""
+    import torch.nn.functional as F
+    S, H, I, L = C3_S, C3_H, C3_I, C3_L
+    qd, kvd = C3_QH * C3_HD, C3_KVH * C3_HD
+    layers = []
+    for _ in range(L):
+        layers.append((rand_weight_dev(clefq, qd + 2 * kvd, H, gen), rand_weight_dev(clefq, H, qd, gen),
+                       rand_weight_dev(clefq, I, H, gen), rand_weight_dev(clefq, I, H, gen),
+                       rand_weight_dev(clefq, H, I, gen),
+                       (torch.randn(H, device="cuda", generator=gen) * 0.02).to(torch.bfloat16),
+                       (torch.randn(H, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)))
+    x0 = torch.randn(S, H, device="cuda", generator=gen).to(torch.bfloat16)
+    ws = torch.empty(clefq.lib().clefq_mlp_workspace_size(S, H, I), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    att_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+
+    def step(record=False):
+        h = x0
+        for li, (wqkv, wo, g, u, d, n1, n2) in enumerate(layers):
+            a = clefq.prepare(h, 4, clefq.stride_for(H), clefq.PREP_NORM, n1)
+            qkv = clefq.project_prepared(S, wqkv, a)
+            if record:
+                att_ev[li][0].record(stream)
+            q = qkv[:, :qd].view(S, C3_QH, C3_HD).transpose(0, 1).unsqueeze(0)
+            k = qkv[:, qd:qd + kvd].view(S, C3_KVH, C3_HD).transpose(0, 1).unsqueeze(0)
+            v = qkv[:, qd + kvd:].view(S, C3_KVH, C3_HD).transpose(0, 1).unsqueeze(0)
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+            attn = o[0].transpose(0, 1).reshape(S, qd)
+            if record:
+                att_ev[li][1].record(stream)
+            h = clefq.project_quantized(attn, wo, residual=h)
+            h = clefq.normalized_mlp(h, n2, g, u, d, workspace=ws)
+        return h
+
+    for _ in range(max(2, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    clefq.status()
+    barrier(world)
+    totals, atts = [], []
+    for _ in range(max(3, min(args.steps, 10))):
+        flush.fill_(1)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        step(record=True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        totals.append(t0.elapsed_time(t1))
+        atts.append(sum(a.elapsed_time(b) for a, b in att_ev))
+    clefq.status()
+    ms = all_max(world, statistics.median(totals))
+    att_ms = all_max(world, statistics.median(atts))
+    int4_ms = ms - att_ms
+    ops = L * 2.0 * S * (H * (qd + 2 * kvd) + qd * H + 3 * H * I)
+    out = {"workload": "C3 INT4 decoder prefill: 28 layers, 2048 tokens, hidden 2560, GQA 32q/8kv x 128, MLP 9728; "
+                       "q|k|v, o, gate, up, down all INT4 (RMSNorm fused into packing; SDPA glue in BF16)",
+           "tokens_per_s": world * S / (ms / 1000), "ms_per_step": ms, "attention_glue_ms": att_ms,
+           "int4_ms": int4_ms, "int4_tokens_per_s": world * S / (int4_ms / 1000),
+           "int_ops_per_step": ops, "frac_of_int8_peak_int4_part": ops / (int4_ms / 1000) / 1e12 / i8_peak,
+           "gpu_launches_per_layer": 8, "parallelism": f"dp{world} (replicas)" if world > 1 else "single GPU",
+           "note": "rotary embeddings left out; the attention glue (torch SDPA, causal, GQA) is timed with CUDA events "
+                   "and reported apart"}
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        from oracle import oracle as o
+        threads = len(os.sched_getaffinity(0))
+        rng = np.random.default_rng(3)
+        tok = 128
+        wqkv, wo = rand_weight_host(rng, qd + 2 * kvd, H), rand_weight_host(rng, H, qd)
+        g, u, d = rand_weight_host(rng, I, H), rand_weight_host(rng, I, H), rand_weight_host(rng, H, I)
+        n1 = o.f32_to_bf16((rng.standard_normal(H) * 0.02).astype(np.float32))
+        xh = o.f32_to_bf16(rng.standard_normal((tok, H)).astype(np.float32))
+        attn_h = o.f32_to_bf16(rng.standard_normal((tok, qd)).astype(np.float32))
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            _, c, sc, _ = o.prepare(xh, 4, o.stride_for(H), o.NORM, n1, threads=threads)
+            o.gemm(c, sc, *wqkv, H, threads=threads)
+            _, c, sc, _ = o.prepare(attn_h, 4, o.stride_for(qd), threads=threads)
+            r = o.gemm(c, sc, *wo, qd, residual=xh, threads=threads)
+            o.normalized_mlp_block(r, n1, g, u, d, threads=threads)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= 5.0 and reps >= 2:
+                break
+        per_layer_s = el / reps * (S / tok)
+        out["cpu_baseline"] = {"value": S / (per_layer_s * L), "unit": "tokens/s", "cores": threads, "kind": "port",
+                               "sample": f"{reps} x one layer's INT4 projections on {tok} tokens ({el:.1f} s), "
+                                         f"scaled x{S // tok} tokens and x{L} layers; attention not included"}
+    del layers
+    return out
+
+
+def run_c5(clefq, gen, flush, args, world, rank, i8_peak):
+    """full-depth MoE prefill -- 48 layers of the C4 MoE layer, each with
+    its own router and expert weights, 8192 tokens per GPU (65,536 at 8 GPUs, 16 experts per
+    GPU), run back to back with the residual added after every layer; the router linear is a
+    BF16 torch matmul inside the step.  N > 1: every layer is one clefq_moe_ep_layer call
+    (experts sharded over the ranks).  The interleaved attention core is not on the INT4 path
+    and is not timed here."""
+    per = MOE_E // world
+    layers = []
+    for _ in range(C5_L):
+        wr = torch.randn(MOE_E, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
+        gate = rand_weight_dev(clefq, per * MOE_I, MOE_H, gen)
+        up = rand_weight_dev(clefq, per * MOE_I, MOE_H, gen)
+        down = rand_weight_dev(clefq, per * MOE_H, MOE_I, gen)
+        layers.append((wr, gate, up, down))
+    x0 = torch.randn(MOE_T, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
+    comm = None
+    if world > 1:
+        from clefq.comm import Comm
+        from clefq.ep import ExpertShard, ep_layer_region_bytes, omni_moe_ep_fused
+        cap = world * MOE_T * MOE_K
+        comm = Comm(ep_layer_region_bytes(MOE_T, MOE_H, MOE_K, world, cap))
+        ws = torch.empty(clefq.lib().clefq_moe_ep_layer_workspace_size(MOE_T, MOE_H, MOE_I, MOE_E, MOE_K, world, cap),
+                         dtype=torch.uint8, device="cuda")
+        shards = [ExpertShard(g, u, d, rank * per, per, MOE_E, MOE_I) for _, g, u, d in layers]
+    else:
+        ws = torch.empty(clefq.lib().clefq_moe_workspace_size(MOE_T, MOE_H, MOE_I, MOE_E, MOE_K), dtype=torch.uint8,
+                         device="cuda")
+    out_buf = torch.empty((MOE_T, MOE_H), dtype=torch.bfloat16, device="cuda")
+
+    def step():
+        h = x0
+        for li, (wr, g, u, d) in enumerate(layers):
+            logits = h @ wr.t()
+            if world > 1:
+                omni_moe_ep_fused(h, logits, shards[li], comm, MOE_K, recv_cap=cap, workspace=ws, out=out_buf)
+            else:
+                clefq._call("clefq_moe", clefq._stream(), clefq._ptr(h), clefq._ptr(logits), clefq.BF16, MOE_T, MOE_H,
+                            MOE_I, MOE_E, MOE_K, clefq._ptr(g.codes), clefq._ptr(g.scales), clefq._ptr(u.codes),
+                            clefq._ptr(u.scales), clefq._ptr(d.codes), clefq._ptr(d.scales), clefq._ptr(out_buf), None,
+                            clefq._ptr(ws), ws.numel())
+            h = h + out_buf
+        return h
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    clefq.status()
+    barrier(world)
+    times = time_steps(step, max(3, min(args.steps, 5)), flush)
+    clefq.status()
+    ms = all_max(world, statistics.median(times))
+    if comm is not None:
+        comm.close()
+    ops = C5_L * 2.0 * MOE_T * MOE_K * (MOE_H * 2 * MOE_I + MOE_I * MOE_H)
+    out = {"workload": f"C5 full-depth MoE prefill: 48 x the C4 MoE layer (own weights per layer), {MOE_T} tokens "
+                       f"per GPU ({world * MOE_T} in all), {per} experts per GPU, residual after each layer",
+           "tokens_per_s": world * MOE_T / (ms / 1000), "ms_per_step": ms, "ms_per_layer": ms / C5_L,
+           "int_ops_per_rank_per_step": ops, "frac_of_int8_peak": ops / (ms / 1000) / 1e12 / i8_peak,
+           "parallelism": f"ep{world}: one clefq_moe_ep_layer call per layer" if world > 1 else "single GPU",
+           "note": "router linear (BF16 torch matmul) and residual add inside the step; the interleaved attention "
+                   "core is not on the INT4 path and not timed"}
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        from oracle import oracle as o
+        threads = len(os.sched_getaffinity(0))
+        rng = np.random.default_rng(5)
+        tok = 512
+        g, u, d = (rand_weight_host(rng, MOE_E * MOE_I, MOE_H), rand_weight_host(rng, MOE_E * MOE_I, MOE_H),
+                   rand_weight_host(rng, MOE_E * MOE_H, MOE_I))
+        xh = o.f32_to_bf16(rng.standard_normal((tok, MOE_H)).astype(np.float32))
+        lg = o.f32_to_bf16((rng.standard_normal((tok, MOE_E)) * 40).astype(np.float32))
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            o.moe_layer(xh, lg, (g[0], g[1], MOE_I), (u[0], u[1], MOE_I), (d[0], d[1], MOE_H), threads=threads)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= 5.0 and reps >= 2:
+                break
+        per_layer_s = el / reps * (MOE_T / tok)
+        out["cpu_baseline"] = {"value": MOE_T / (per_layer_s * C5_L), "unit": "tokens/s", "cores": threads,
+                               "kind": "port", "sample": f"{reps} x one C4 MoE layer on {tok} tokens ({el:.1f} s), "
+                                                         f"scaled x{MOE_T // tok} tokens and x{C5_L} layers"}
+    del layers
     return out
 
 
@@ -550,6 +740,8 @@ def run_clefq(args, world, rank, local):
     c1 = None
     if not args.skip_c1:
         c1 = run_c1(clefq, gen, flush, args, world, rank, i8_peak)
+    c3 = None if args.skip_c3 else run_c3(clefq, gen, flush, args, world, rank, i8_peak)
+    c5 = None if args.skip_c5 else run_c5(clefq, gen, flush, args, world, rank, i8_peak)
 
     launches = 4 * args.steps
     line = {
@@ -582,6 +774,10 @@ def run_clefq(args, world, rank, local):
     }
     if c1:
         line["c1"] = c1
+    if c3:
+        line["c3"] = c3
+    if c5:
+        line["c5"] = c5
     if moe:
         line["secondary"] = moe
     if tp:
@@ -606,6 +802,8 @@ def main():
     ap.add_argument("--skip-tp", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-c1", action="store_true")
+    ap.add_argument("--skip-c3", action="store_true")
+    ap.add_argument("--skip-c5", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0,
                     help="calls in the timed e2e stream (default: --steps clamped to [100, 200]); "
                          "small values keep profiler captures short")
