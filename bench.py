@@ -395,10 +395,9 @@ def run_c3(clefq, gen, flush, args, world, rank, i8_peak):
 def run_c5(clefq, gen, flush, args, world, rank, i8_peak):
     """full-depth MoE prefill -- 48 layers of the C4 MoE layer, each with
     its own router and expert weights, 8192 tokens per GPU (65,536 at 8 GPUs, 16 experts per
-    GPU), run back to back with the residual added after every layer; the router linear is a
-    BF16 torch matmul inside the step.  N > 1: every layer is one clefq_moe_ep_layer call
-    (experts sharded over the ranks).  The interleaved attention core is not on the INT4 path
-    and is not timed here."""
+    GPU), run back to back with the residual added after every layer.  N > 1: every layer is one clefq_moe_ep_layer call
+    (experts sharded over the ranks).  The router linear runs fused with the router inside each
+    layer.  The interleaved attention core is not on the INT4 path and is not timed here."""
     per = MOE_E // world
     layers = []
     for _ in range(C5_L):
@@ -425,14 +424,11 @@ def run_c5(clefq, gen, flush, args, world, rank, i8_peak):
     def step():
         h = x0
         for li, (wr, g, u, d) in enumerate(layers):
-            logits = h @ wr.t()
             if world > 1:
-                omni_moe_ep_fused(h, logits, shards[li], comm, MOE_K, recv_cap=cap, workspace=ws, out=out_buf)
+                omni_moe_ep_fused(h, None, shards[li], comm, MOE_K, recv_cap=cap, workspace=ws, out=out_buf,
+                                  router_weight=wr)
             else:
-                clefq._call("clefq_moe", clefq._stream(), clefq._ptr(h), clefq._ptr(logits), clefq.BF16, MOE_T, MOE_H,
-                            MOE_I, MOE_E, MOE_K, clefq._ptr(g.codes), clefq._ptr(g.scales), clefq._ptr(u.codes),
-                            clefq._ptr(u.scales), clefq._ptr(d.codes), clefq._ptr(d.scales), clefq._ptr(out_buf), None,
-                            clefq._ptr(ws), ws.numel())
+                clefq.omni_moe(h, None, g, u, d, workspace=ws, router_weight=wr, out=out_buf)
             h = h + out_buf
         return h
 
@@ -452,8 +448,8 @@ def run_c5(clefq, gen, flush, args, world, rank, i8_peak):
            "tokens_per_s": world * MOE_T / (ms / 1000), "ms_per_step": ms, "ms_per_layer": ms / C5_L,
            "int_ops_per_rank_per_step": ops, "frac_of_int8_peak": ops / (ms / 1000) / 1e12 / i8_peak,
            "parallelism": f"ep{world}: one clefq_moe_ep_layer call per layer" if world > 1 else "single GPU",
-           "note": "router linear (BF16 torch matmul) and residual add inside the step; the interleaved attention "
-                   "core is not on the INT4 path and not timed"}
+           "note": "router linear fused with the router and residual add inside the step; the interleaved "
+                   "attention core is not on the INT4 path and not timed"}
     if rank == 0 and world == 1 and not args.skip_cpu:
         from oracle import oracle as o
         threads = len(os.sched_getaffinity(0))
@@ -597,7 +593,9 @@ def run_clefq(args, world, rank, local):
     if not args.skip_moe:
         mx = torch.randn(MOE_T, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
         wr = torch.randn(MOE_E, MOE_H, device="cuda", generator=gen).to(torch.bfloat16)
-        logits = mx @ wr.t()     # router linear (BF16, cuBLAS): outside the INT4 path
+        # the NCCL composition routes from precomputed logits; the fused layers take the
+        # router weight and run the router linear fused with the router inside the layer
+        logits = mx @ wr.t()
         # The expert weights are the same on every rank (one seed): rank r keeps its slice, and
         # the full set gives the single-GPU result each rank's expert-parallel output must equal.
         wgen = torch.Generator(device="cuda")
@@ -625,23 +623,24 @@ def run_clefq(args, world, rank, local):
             # parity before timing: both expert-parallel paths against clefq_moe on one GPU
             ref = clefq.omni_moe(mx, logits, mg, mu, md, workspace=mws)
             nccl_out = nstep()[0]
-            omni_moe_ep_fused(mx, logits, shard, ecomm, MOE_K, recv_cap=cap, workspace=ews, out=eout)
+            omni_moe_ep_fused(mx, None, shard, ecomm, MOE_K, recv_cap=cap, workspace=ews, out=eout, router_weight=wr)
+            ref_fused = clefq.omni_moe(mx, None, mg, mu, md, workspace=mws, router_weight=wr)
             torch.cuda.synchronize()
             clefq.status()
-            same = torch.equal(eout.view(torch.int16), ref.view(torch.int16)) and \
+            same = torch.equal(eout.view(torch.int16), ref_fused.view(torch.int16)) and \
                 torch.equal(nccl_out.view(torch.int16), ref.view(torch.int16))
             parity = all_min(world, same)
-            del ref, nccl_out
+            del ref, nccl_out, ref_fused
             for _ in range(3):
                 nstep()
             torch.cuda.synchronize()
             barrier(world)
             nt = time_steps(nstep, max(5, min(args.steps, 30)), flush)
             nccl_ms = all_max(world, sum(nt) / len(nt))
-            mstep = lambda: omni_moe_ep_fused(mx, logits, shard, ecomm, MOE_K, recv_cap=cap,  # noqa: E731
-                                              workspace=ews, out=eout)
+            mstep = lambda: omni_moe_ep_fused(mx, None, shard, ecomm, MOE_K, recv_cap=cap,  # noqa: E731
+                                              workspace=ews, out=eout, router_weight=wr)
         else:
-            mstep = lambda: clefq.omni_moe(mx, logits, mg, mu, md, workspace=mws)   # noqa: E731
+            mstep = lambda: clefq.omni_moe(mx, None, mg, mu, md, workspace=mws, router_weight=wr)   # noqa: E731
         for _ in range(3):
             mstep()
         torch.cuda.synchronize()
@@ -662,7 +661,8 @@ def run_clefq(args, world, rank, local):
         else:
             # the whole layer against the int8 tensor peak (its GEMMs are 0.62 T int ops), and
             # the dominant launch -- the grouped gate|up expert GEMM -- timed alone below
-            moe_roof = {"bound": "tensor", "kernel": "the whole clefq_moe layer (7 launches)",
+            moe_roof = {"bound": "tensor", "kernel": "the whole clefq_moe layer (7 launches, router linear fused "
+                                                  "with the router)",
                         "achieved": ops / (mms / 1000) / 1e12, "peak": i8_peak, "unit": "TOP/s",
                         "frac": ops / (mms / 1000) / 1e12 / i8_peak, "algorithmic_ops": ops,
                         "traffic": traffic_tab.get("moe_c4_layer", {}).get("traffic_bytes")}
@@ -673,6 +673,8 @@ def run_clefq(args, world, rank, local):
                else "single GPU", "tokens_per_s": world * MOE_T / (mms / 1000), "ms_per_step": mms,
                "nccl_all_to_all_ms_per_step": nccl_ms,
                "parity": parity,
+               "router": "router linear fused with the router (clefq_route_linear's kernel) inside the timed "
+                         "layer; the NCCL composition routes from precomputed logits",
                "parity_note": "each rank's fused and NCCL expert-parallel outputs equal clefq_moe over the same "
                               "tokens with all 128 experts on one GPU, bit for bit (all ranks)" if world > 1 else
                               "tests/test_gpu_fullsize.py checks this layer at full size against the CPU oracle",

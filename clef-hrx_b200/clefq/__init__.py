@@ -19,7 +19,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libclefq.so")
 
 PREP_PLAIN, PREP_SWIGLU, PREP_ATTN_GATE, PREP_NORM, PREP_NORM_STORE = 0, 1, 2, 3, 4
-BF16, F32 = 0, 1
+BF16, F32, ROUTER_WEIGHT_BF16 = 0, 1, 2
 EXPERTS, TOP_K = 128, 8
 
 ERRORS = {-1: "shape", -2: "alignment", -3: "cuda", -4: "nccl", -5: "timeout", -6: "workspace"}
@@ -38,6 +38,7 @@ _SYMBOLS = {
     "clefq_gemm_pair_s8": (ctypes.c_int, ["p", "p", "l", "p", "l", "p", "p", "p", "p", "l", "l", "p", "l"]),
     "clefq_swiglu": (ctypes.c_int, ["p", "p", "p", "l", "p"]),
     "clefq_route": (ctypes.c_int, ["p", "p", "i", "l", "i", "i", "p"]),
+    "clefq_route_linear": (ctypes.c_int, ["p", "p", "p", "l", "l", "i", "i", "p", "p"]),
     "clefq_group_workspace_size": (ctypes.c_int64, ["l", "i", "i"]),
     "clefq_group_routes": (ctypes.c_int, ["p", "p", "l", "i", "i", "p", "p", "p", "l"]),
     "clefq_expert_tasks": (ctypes.c_int, ["p", "p", "l", "i", "p"]),
@@ -393,6 +394,23 @@ def omni_route(logits, topk=TOP_K):
     return out
 
 
+def omni_route_linear(x, router_weight, topk=TOP_K, logits_out=False):
+    """Router linear (BF16 projection by mlp.gate) and omni_route in one kernel
+    (src/omni.rs:760-765) -> routes f32 [tokens][2*topk], and the BF16 logits if asked."""
+    _need_cuda(x, router_weight)
+    if x.dtype != torch.bfloat16 or router_weight.dtype != torch.bfloat16 or x.dim() != 2 or \
+            router_weight.dim() != 2 or x.shape[1] != router_weight.shape[1]:
+        raise ValueError("router linear shape/dtype mismatch")
+    tokens, hidden = x.shape
+    experts = router_weight.shape[0]
+    x, router_weight = x.contiguous(), router_weight.contiguous()
+    routes = torch.empty((tokens, 2 * topk), dtype=torch.float32, device=x.device)
+    logits = torch.empty((tokens, experts), dtype=torch.bfloat16, device=x.device) if logits_out else None
+    _call("clefq_route_linear", _stream(), _ptr(x), _ptr(router_weight), tokens, hidden, experts, topk, _ptr(routes),
+          _ptr(logits))
+    return (routes, logits) if logits_out else routes
+
+
 def omni_group_routes_ordered(routes, experts=EXPERTS):
     """src/omni.rs:213-245 -> (groups f32 [experts][tokens+1], order f32 [tokens][topk])."""
     tokens, width = routes.shape
@@ -461,15 +479,22 @@ def omni_combine(values, routes):
 
 
 def omni_moe(x, logits, gate: QuantizedWeight, up: QuantizedWeight, down: QuantizedWeight, experts=EXPERTS,
-             topk=TOP_K, workspace=None, routes_out=None):
-    """The MoE block of forward_layers_cached (src/omni.rs:761-857), one C-ABI call."""
+             topk=TOP_K, workspace=None, routes_out=None, router_weight=None, out=None):
+    """The MoE block of forward_layers_cached (src/omni.rs:761-857), one C-ABI call.  Pass
+    router_weight (BF16 [experts][hidden]) instead of logits to fuse the router linear in."""
     tokens, hidden = x.shape
     inter = gate.rows // experts
-    out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=x.device)
+    if out is None:
+        out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=x.device)
     need = lib().clefq_moe_workspace_size(tokens, hidden, inter, experts, topk)
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
-    dt = F32 if logits.dtype == torch.float32 else BF16
+    if router_weight is not None:
+        if logits is not None or router_weight.shape != (experts, hidden):
+            raise ValueError("pass either logits or a router weight [experts][hidden]")
+        logits, dt = router_weight.contiguous(), ROUTER_WEIGHT_BF16
+    else:
+        dt = F32 if logits.dtype == torch.float32 else BF16
     _call("clefq_moe", _stream(), _ptr(x), _ptr(logits), dt, tokens, hidden, inter, experts, topk, _ptr(gate.codes),
           _ptr(gate.scales), _ptr(up.codes), _ptr(up.scales), _ptr(down.codes), _ptr(down.scales), _ptr(out),
           _ptr(routes_out), _ptr(workspace), need)

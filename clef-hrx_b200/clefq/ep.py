@@ -171,13 +171,18 @@ def ep_layer_region_bytes(tokens: int, hidden: int, topk: int, world: int, recv_
 
 
 def omni_moe_ep_fused(x: torch.Tensor, logits: torch.Tensor, shard: ExpertShard, comm, topk: int = 8,
-                      recv_cap: int | None = None, workspace=None, out=None):
+                      recv_cap: int | None = None, workspace=None, out=None, router_weight=None):
     """Expert-parallel Omni MoE block in one C-ABI call (clefq_moe_ep_layer) over a
     `clefq.comm.Comm`: records and products are stored straight into the other ranks'
     symmetric buffers by the dispatch kernel and the expert down-GEMM epilogue, with no host
     synchronisation.  recv_cap (the same on every rank) defaults to world * tokens * topk, which
-    always suffices when every rank has `tokens` tokens.  Returns (out, routes)."""
-    from . import BF16, F32, _call, _need_cuda, _ptr, _stream, lib
+    always suffices when every rank has `tokens` tokens.  Pass router_weight (BF16 [experts]
+    [hidden]) with logits=None to fuse the router linear in.  Returns (out, routes)."""
+    from . import BF16, F32, ROUTER_WEIGHT_BF16, _call, _need_cuda, _ptr, _stream, lib
+    if router_weight is not None:
+        if logits is not None:
+            raise ValueError("pass either logits or a router weight")
+        logits = router_weight
     _need_cuda(x, logits)
     tokens, hidden = x.shape
     world = comm.world
@@ -187,7 +192,7 @@ def omni_moe_ep_fused(x: torch.Tensor, logits: torch.Tensor, shard: ExpertShard,
         recv_cap = world * tokens * topk
     x = x.contiguous()
     logits = logits.contiguous()
-    dt = F32 if logits.dtype == torch.float32 else BF16
+    dt = ROUTER_WEIGHT_BF16 if router_weight is not None else (F32 if logits.dtype == torch.float32 else BF16)
     need = lib().clefq_moe_ep_layer_workspace_size(tokens, hidden, shard.inter, shard.experts, topk, world, recv_cap)
     if need < 0:
         raise ValueError("unsupported expert-parallel MoE layer shape")

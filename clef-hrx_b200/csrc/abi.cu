@@ -14,6 +14,8 @@ int launch_group(const float *routes, int64_t tokens, int topk, int experts, int
                  int *tile_list, int *perm, float *groups, float *order, float *tasks, cudaStream_t stream,
                  int num_sms);
 int launch_tasks(const float *groups, int64_t tokens, int experts, float *tasks, cudaStream_t stream);
+int launch_route_linear(const void *x, const void *w, int64_t tokens, int hidden, int experts, int topk, float *routes,
+                        uint16_t *logits_out, int *err, cudaStream_t stream);
 int launch_groups_to_sorted(const float *groups, int64_t tokens, int topk, int experts, int tile_rows, int *offsets,
                             int *perm, int *tile_list, cudaStream_t stream);
 int launch_gather(const uint8_t *src, int64_t src_ld, const int *perm, int div, int64_t rows, int64_t row_bytes,
@@ -363,6 +365,41 @@ int64_t clefq_group_workspace_size(int64_t tokens, int topk, int experts) {
   Arena a{nullptr, INT64_MAX};
   a = group_tables(a, tokens, topk, experts, &c, &o, &t, &p);
   return aligned_total(a);
+}
+
+// The MoE blocks' router step: logits given (BF16 or F32), or CLEFQ_ROUTER_WEIGHT_BF16: `logits`
+// is the router weight [experts][hidden] and the fused router linear computes them from x.
+static int route_step(const void *x, const void *logits, int logits_dtype, int64_t tokens, int64_t hidden,
+                      int experts, int topk, float *routes, cudaStream_t s) {
+  if (logits_dtype == CLEFQ_ROUTER_WEIGHT_BF16) {
+    if (hidden % 64 || experts < 32 || experts % 32 || topk > 8 || !al16(x) || !al16(logits))
+      return set_err(CLEFQ_ERR_SHAPE, "the fused router needs hidden %% 64 == 0, experts a multiple of 32 and "
+                                      "topk <= 8");
+    int *status = device_status_word();
+    if (!status) return cuda_err("status word");
+    return launch_route_linear(x, logits, tokens, (int)hidden, experts, topk, routes, nullptr, status, s)
+               ? cuda_err("fused router launch")
+               : 0;
+  }
+  if (logits_dtype != CLEFQ_BF16 && logits_dtype != CLEFQ_F32) return set_err(CLEFQ_ERR_SHAPE, "logits dtype");
+  return launch_route(logits, logits_dtype == CLEFQ_F32, tokens, experts, topk, routes, s) ? cuda_err("routing launch")
+                                                                                          : 0;
+}
+
+int clefq_route_linear(void *stream, const void *x, const void *router_weight, int64_t tokens, int64_t hidden,
+                       int experts, int topk, float *routes, void *logits_out) {
+  if (tokens < 0 || tokens > 16777216 || hidden < 64 || hidden > 65536 || hidden % 64 || experts < 32 ||
+      experts > 128 || experts % 32 || topk < 1 || topk > 8)
+    return set_err(CLEFQ_ERR_SHAPE, "invalid fused router shape (hidden %% 64, experts 32..128 in steps of 32, "
+                                    "topk 1..8)");
+  if (tokens == 0) return 0;
+  if (!al16(x) || !al16(router_weight) || (logits_out && !al16(logits_out)))
+    return set_err(CLEFQ_ERR_ALIGN, "router inputs and logits must be 16-byte aligned");
+  int *status = device_status_word();
+  if (!status) return cuda_err("status word");
+  const int rc = launch_route_linear(x, router_weight, tokens, (int)hidden, experts, topk, routes,
+                                     static_cast<uint16_t *>(logits_out), status, static_cast<cudaStream_t>(stream));
+  return rc ? cuda_err("fused router launch") : 0;
 }
 
 int clefq_group_routes(void *stream, const float *routes, int64_t tokens, int topk, int experts, float *groups,
@@ -804,8 +841,8 @@ int clefq_moe(void *stream, const void *x, const void *logits, int logits_dtype,
   if (gemm_tile_rows((int)hidden, (int)(hidden / 128)) != tile_rows) {
     return set_err(CLEFQ_ERR_SHAPE, "hidden and intermediate must both be multiples of 256, or neither");
   }
-  int rc = launch_route(logits, logits_dtype == CLEFQ_F32, tokens, experts, topk, routes, s);
-  if (rc) return cuda_err("routing launch");
+  int rc = route_step(x, logits, logits_dtype, tokens, hidden, experts, topk, routes, s);
+  if (rc) return rc;
   // the stable grouping also gives every route its expert-sorted row (slots; -1 for a route
   // left out), so packing x can write each token's operand straight to its routes' rows
   if (cudaMemsetAsync(t.slots, 0xff, sizeof(int) * nroutes, s) != cudaSuccess) return cuda_err("slot reset");
@@ -1046,7 +1083,7 @@ int clefq_moe_ep_layer(clefq_comm *c, void *stream, const void *x, const void *l
   const int world = c->world, rank = c->rank;
   int rc = check_ep_layer(tokens, hidden, inter, experts, topk, world, recv_cap);
   if (rc) return rc;
-  if (logits_dtype != CLEFQ_BF16 && logits_dtype != CLEFQ_F32) return set_err(CLEFQ_ERR_SHAPE, "logits dtype");
+  if (logits_dtype != CLEFQ_BF16 && logits_dtype != CLEFQ_F32 && logits_dtype != CLEFQ_ROUTER_WEIGHT_BF16) return set_err(CLEFQ_ERR_SHAPE, "logits dtype");
   if ((tokens > 0 && (!x || !logits || !out)) || (tokens > 0 && (!al16(x) || !al16(out))))
     return set_err(CLEFQ_ERR_ALIGN, "x and out must be 16-byte aligned");
   const int local = experts / world;
@@ -1075,8 +1112,8 @@ int clefq_moe_ep_layer(clefq_comm *c, void *stream, const void *x, const void *l
   int *my_counts = counts + rank * world;
   // 1. route and pack this rank's tokens; plan: routes grouped by destination rank
   if (tokens > 0) {
-    rc = launch_route(logits, logits_dtype == CLEFQ_F32, tokens, experts, topk, routes, s);
-    if (rc) return cuda_err("route launch");
+    rc = route_step(x, logits, logits_dtype, tokens, hidden, experts, topk, routes, s);
+    if (rc) return rc;
     rc = run_prepare(s, CLEFQ_PREP_PLAIN, 4, x, hidden, nullptr, 0, tokens, hidden, sh, t.xq, nullptr, 0, nullptr, 0);
     if (rc) return rc;
   }

@@ -50,7 +50,13 @@ typedef enum {
   CLEFQ_PREP_NORM_STORE = 4 /* h3_prepare_norm_store_i*: also writes the BF16 normalized rows */
 } clefq_prep_kind_t;
 
-typedef enum { CLEFQ_BF16 = 0, CLEFQ_F32 = 1 } clefq_dtype_t;
+typedef enum {
+  CLEFQ_BF16 = 0,
+  CLEFQ_F32 = 1,
+  /* MoE blocks only (clefq_moe, clefq_moe_ep_layer): the `logits` argument is the router weight
+   * BF16 [experts][hidden]; the blocks then route with clefq_route_linear's fused kernel on x */
+  CLEFQ_ROUTER_WEIGHT_BF16 = 2
+} clefq_dtype_t;
 
 CLEFQ_API const char *clefq_last_error(void);
 CLEFQ_API int clefq_version(void);
@@ -175,6 +181,21 @@ CLEFQ_API int clefq_route(void *stream, const void *logits, int logits_dtype, in
                           float *routes);
 
 /*
+ * Router linear and router in one kernel; replaces the two steps of the MoE block
+ * (src/omni.rs:760-765): logits = project(norm, "mlp.gate") (BF16 GEMM, f32 accumulation,
+ * BF16 output) followed by omni_route(logits, topk).
+ *   x              BF16 [tokens][hidden] (the normalised hidden rows)
+ *   router_weight  BF16 [experts][hidden], row-major
+ *   routes         f32 [tokens][2*topk], as clefq_route
+ *   logits_out     BF16 [tokens][experts] or NULL: the logits the routes were chosen from
+ * The logits' f32 accumulation order is this kernel's (a tcgen05 BF16 GEMM), so they can
+ * differ from another GEMM's by one BF16 rounding; routes are always exactly clefq_route of
+ * logits_out.  Checks: hidden % 64 == 0; experts in 32..128, a multiple of 32; topk 1..8.
+ */
+CLEFQ_API int clefq_route_linear(void *stream, const void *x, const void *router_weight, int64_t tokens,
+                                 int64_t hidden, int experts, int topk, float *routes, void *logits_out);
+
+/*
  * Stable grouping; replaces omni_group_routes / omni_group_routes_ordered
  * (src/omni.rs:192-245, kernels/omni_group_routes{,_ordered}.loom):
  *   groups f32 [experts][tokens+1] = count, then route ids t*topk+rank in token order
@@ -271,7 +292,8 @@ CLEFQ_API int clefq_mlp_host(void *stream, const void *x_host, int64_t m, int64_
  * Omni INT4 MoE block; replaces the expert part of forward_layers_cached
  * (src/omni.rs:761-857, fast defaults): route(logits) -> ordered groups -> gate, up
  * experts on the shared packed input -> SwiGLU -> down experts -> ordered combine.
- *   x BF16 [tokens][hidden] (normalized input), logits [tokens][experts] (logits_dtype)
+ *   x BF16 [tokens][hidden] (normalized input), logits [tokens][experts] (logits_dtype), or
+ *   with CLEFQ_ROUTER_WEIGHT_BF16 the router weight [experts][hidden] (router linear fused in)
  *   gate/up tiled [experts*inter][hidden] + scales; down tiled [experts*hidden][inter]
  *   out BF16 [tokens][hidden]; routes_out f32 [tokens][2*topk] (nullable)
  * workspace >= clefq_moe_workspace_size(tokens, hidden, inter, experts, topk).
