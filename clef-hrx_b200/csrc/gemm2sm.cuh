@@ -69,7 +69,7 @@ struct Smem2 {
 
 struct TileMap2 {
   int n_pairs, total;
-  int span;  // token rows per pair tile (dense): SUB x BN2
+  int span;  // token rows per pair tile: SUB x BN2 (dense two-stage), BN2 (grouped), or the deep kernel's tile
   CQ_DEV bool get(const GemmParams &p, int t, int64_t &row0, int &rows_valid, int &np, int &expert) const {
     if (t >= total) return false;
     const int mt = t / n_pairs;
@@ -78,7 +78,7 @@ struct TileMap2 {
       expert = p.tile_list[1 + 2 * mt];
       row0 = p.tile_list[2 + 2 * mt];
       const int64_t end = p.expert_offsets[expert + 1];
-      rows_valid = (int)(end - row0 < BN2 ? end - row0 : BN2);
+      rows_valid = (int)(end - row0 < span ? end - row0 : span);
     } else {
       expert = 0;
       row0 = (int64_t)mt * span;
