@@ -44,6 +44,8 @@ _SYMBOLS = {
     "clefq_expert_tasks": (ctypes.c_int, ["p", "p", "l", "i", "p"]),
     "clefq_expert_workspace_size": (ctypes.c_int64, ["l", "i", "i", "l"]),
     "clefq_expert": (ctypes.c_int, ["p", "p", "l", "p", "p", "p", "p", "l", "i", "i", "l", "l", "i", "p", "p", "l"]),
+    "clefq_expert_gate_up": (ctypes.c_int, ["p", "p", "l", "p", "p", "p", "p", "p", "p", "l", "i", "i", "l", "l", "p",
+                                            "p", "l"]),
     "clefq_combine": (ctypes.c_int, ["p", "p", "p", "p", "l", "i", "l", "p"]),
     "clefq_mlp_workspace_size": (ctypes.c_int64, ["l", "l", "l"]),
     "clefq_mlp": (ctypes.c_int, ["p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p", "p", "p", "l"]),
@@ -458,6 +460,25 @@ def omni_expert(x_prepared: Prepared, routes, groups, w: QuantizedWeight, input_
     _call("clefq_expert", _stream(), _ptr(x_prepared.codes), x_prepared.codes.shape[1], _ptr(x_prepared.scales),
           _ptr(w.codes), _ptr(w.scales), _ptr(groups), tokens, topk, experts, k, n, int(input_routed), _ptr(out),
           _ptr(ws), need)
+    return out
+
+
+def omni_gate_up(x_prepared: Prepared, routes, groups, gate: QuantizedWeight, up: QuantizedWeight,
+                 experts=EXPERTS):
+    """src/omni.rs:302-373 fused gate/up experts: hidden[route] = bf16(bf16(silu(g)) * u),
+    SwiGLU in the GEMM epilogue -> BF16 [tokens*topk][n] in route order."""
+    tokens, width = routes.shape
+    topk = width // 2
+    n = gate.rows // experts
+    k = gate.cols
+    if up.rows != gate.rows or up.cols != k:
+        raise ValueError("gate and up expert weights differ in shape")
+    out = torch.empty((tokens * topk, n), dtype=torch.bfloat16, device=routes.device)
+    need = lib().clefq_expert_workspace_size(tokens, topk, experts, k)
+    ws = torch.empty(need, dtype=torch.uint8, device=routes.device)
+    _call("clefq_expert_gate_up", _stream(), _ptr(x_prepared.codes), x_prepared.codes.shape[1],
+          _ptr(x_prepared.scales), _ptr(gate.codes), _ptr(gate.scales), _ptr(up.codes), _ptr(up.scales), _ptr(groups),
+          tokens, topk, experts, k, n, _ptr(out), _ptr(ws), need)
     return out
 
 

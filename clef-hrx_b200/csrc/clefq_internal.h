@@ -46,6 +46,7 @@ struct PrepareArgs {
   int narrow;           // set by the launcher: GEMM-input rows of 1..3 groups, one team per group
 };
 int launch_prepare(const PrepareArgs &a, cudaStream_t stream);
+const uint16_t *silu_table_device();  // the BF16 SiLU table on the current device
 int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);
 int launch_retile(const uint32_t *codes, int64_t rows, int64_t in_words, int64_t words, uint32_t *out,
                   cudaStream_t stream, int num_sms);
@@ -94,8 +95,15 @@ struct GemmParams {
   const int *ret_row;
   const float *ret_prob;
   int store16;              // set by launch_gemm: every output address allows 16-byte stores
+  // SwiGLU epilogue (int4, two weight maps: gate in w[0], up in w[1]; deep-ring kernel only):
+  // each CTA computes 64 gate and the matching 64 up rows of one hidden-column slab and stores
+  // bf16(bf16(silu(gate)) * up) -- the reference's SwiGLU of the two BF16 projections -- as
+  // hidden [rows][ldo] BF16, n / 2 columns; silu_tab is the BF16 SiLU table of every input.
+  int swiglu;
+  const uint16_t *silu_tab;
 };
 int launch_gemm(const GemmParams &p, cudaStream_t stream);
+bool gemm_swiglu_ok(int64_t n_each, int64_t k);  // the SwiGLU epilogue serves this gate|up shape
 // Token rows per tile of the kernel launch_gemm picks for this output shape (grouped
 // callers build their tile lists with it).
 int gemm_tile_rows(int n, int n_split);

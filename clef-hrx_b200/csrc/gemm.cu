@@ -398,6 +398,19 @@ static bool weight_map(EncodeTiledFn enc, CUtensorMap *m, const uint32_t *w, int
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The same weight tiles with one box = 64 rows of one block (the SwiGLU epilogue's gate or up
+// half of a CTA's 128 weight rows), 8 KB, 128-byte swizzled.
+static bool weight_map_half(EncodeTiledFn enc, CUtensorMap *m, const uint32_t *w, int64_t rows, int k) {
+  const int64_t blocks = rows / 128 * (k / 256);
+  cuuint64_t dims[3] = {32, 128, (cuuint64_t)blocks};
+  cuuint64_t strides[2] = {128, 16384};
+  cuuint32_t box[3] = {32, 64, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint32_t *>(w), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // The same weight tiles with one box = one whole block (int4) or two consecutive blocks
 // (int8): 16 or 32 KB contiguous, 128-byte swizzled.
 static bool weight_map_blocks(EncodeTiledFn enc, CUtensorMap *m, const uint32_t *w, int64_t rows, int k, int bits) {
@@ -481,6 +494,12 @@ static cudaError_t launch_deep_2sm(int64_t pair_tiles, const CUtensorMap &t, con
 }
 
 bool gemm_uses_pairs(const GemmParams &p) { return p.n_split % 2 == 0 && p.n % 256 == 0; }
+
+// Whether launch_gemm can apply the SwiGLU epilogue to a gate|up launch of n_each rows per
+// weight matrix and depth k: int4 on the deep-ring kernel.
+bool gemm_swiglu_ok(int64_t n_each, int64_t k) {
+  return CLEFQ_GEMM_DEEP && n_each % 256 == 0 && k % 256 == 0 && k / 256 >= 8 && silu_table_device() != nullptr;
+}
 int gemm_tile_rows(int n, int n_split) { return (n_split % 2 == 0 && n % 256 == 0) ? two_sm::BN2 : BN; }
 
 static bool allows_store16(const GemmParams &p) {
@@ -509,6 +528,7 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
   const bool pairs = gemm_uses_pairs(p);
   if (p.n_out_peer && (!pairs || p.grouped || !p.out || p.n_out_peer > kMaxPeers)) return CLEFQ_ERR_SHAPE;
   if (p.ret_row && (!pairs || !p.grouped || !p.scatter || !p.ret_rank || !p.ret_prob)) return CLEFQ_ERR_SHAPE;
+  if (p.swiglu && (!pairs || p.bits != 4)) return CLEFQ_ERR_SHAPE;
   for (int d = 0; d < p.n_out_peer; ++d)
     if ((uintptr_t)p.out_peer[d] % 8) return CLEFQ_ERR_ALIGN;
   const int tile_rows = pairs ? two_sm::BN2 : BN;
@@ -556,12 +576,21 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return CLEFQ_ERR_CUDA;
-    // weights: whole 128-row x 32-word blocks (int8: the two blocks of a K=256 slice)
-    if (!weight_map_blocks(enc, &wmap0, p.w[0], wrows, p.k, p.bits)) return CLEFQ_ERR_CUDA;
-    if (two) {
-      if (!weight_map_blocks(enc, &wmap1, p.w[1], wrows, p.k, p.bits)) return CLEFQ_ERR_CUDA;
+    if (p.swiglu) {
+      // the SwiGLU epilogue pairs gate and up rows of the same hidden columns in one CTA
+      if (!deep || !two || p.residual || p.out_f32 || p.n_out_peer || p.ret_row || (p.scatter && !p.grouped) ||
+          !p.out || !p.silu_tab || p.ldo % 2)
+        return CLEFQ_ERR_SHAPE;
+      if (!weight_map_half(enc, &wmap0, p.w[0], wrows, p.k) || !weight_map_half(enc, &wmap1, p.w[1], wrows, p.k))
+        return CLEFQ_ERR_CUDA;
     } else {
-      wmap1 = wmap0;
+      // weights: whole 128-row x 32-word blocks (int8: the two blocks of a K=256 slice)
+      if (!weight_map_blocks(enc, &wmap0, p.w[0], wrows, p.k, p.bits)) return CLEFQ_ERR_CUDA;
+      if (two) {
+        if (!weight_map_blocks(enc, &wmap1, p.w[1], wrows, p.k, p.bits)) return CLEFQ_ERR_CUDA;
+      } else {
+        wmap1 = wmap0;
+      }
     }
     const int64_t pair_tiles = tiles_m * (p.n / two_sm::BMP);
     cudaError_t e;

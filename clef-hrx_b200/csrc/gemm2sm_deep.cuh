@@ -165,7 +165,15 @@ __global__ void __launch_bounds__(DeepCfg<BN>::THREADS, 1)
           const int sw = g % NW, st = g % NT;
           if (!(ok = mbar_wait_bounded(&s.wsm_empty[sw], ((g / NW) & 1) ^ 1, &s.err, 1))) break;
           mbar_arrive_expect_tx(&s.wsm_full[sw], W_BYTES);
-          tma_load_3d(ring + W_OFF + sw * W_BYTES, w_map, &s.wsm_full[sw], 0, 0, w_row_tile * blocks_k + kb);
+          if (p.swiglu) {
+            // 64 gate rows, then the 64 up rows of the same hidden columns: the converters'
+            // rows 0-63 and 64-127 (each box keeps the 128-byte swizzle of its rows)
+            const int blk = (expert * p.n_split + np) * blocks_k + kb;
+            tma_load_3d(ring + W_OFF + sw * W_BYTES, &w_map0, &s.wsm_full[sw], 0, 64 * (int)rank, blk);
+            tma_load_3d(ring + W_OFF + sw * W_BYTES + W_BYTES / 2, &w_map1, &s.wsm_full[sw], 0, 64 * (int)rank, blk);
+          } else {
+            tma_load_3d(ring + W_OFF + sw * W_BYTES, w_map, &s.wsm_full[sw], 0, 0, w_row_tile * blocks_k + kb);
+          }
           if (!(ok = mbar_wait_bounded(&s.tok_empty[st], ((g / NT) & 1) ^ 1, &s.err, 1))) break;
           if (rank == 0) mbar_arrive_expect_tx(&s.tok_full[st], 2 * TOK_B);
           tma_load_3d_cg2(ring + st * TOK_B, &tok_map, mapa_shared(smem_u32(&s.tok_full[st]), 0), 0,
@@ -353,10 +361,18 @@ __global__ void __launch_bounds__(DeepCfg<BN>::THREADS, 1)
           }
         }
       }
-      int which, w_row_tile;
-      weight_tile(np, expert, which, w_row_tile);
-      const float ws = p.w_scales[which][(int64_t)w_row_tile * 128 + r];
-      const int col0 = (2 * np + (int)rank) * 128;  // first output column of this CTA
+      float ws;
+      int col0;  // first output column of this CTA
+      if (p.swiglu) {
+        // TMEM lanes 0-63: gate rows, 64-127: up rows of hidden columns col0 .. col0 + 63
+        col0 = np * 128 + 64 * (int)rank;
+        ws = p.w_scales[r >> 6][(int64_t)expert * p.n_split * 128 + col0 + (r & 63)];
+      } else {
+        int which, w_row_tile;
+        weight_tile(np, expert, which, w_row_tile);
+        ws = p.w_scales[which][(int64_t)w_row_tile * 128 + r];
+        col0 = (2 * np + (int)rank) * 128;
+      }
       if (!GROUPED && p.out_f32) {
         // F32 output: the reference's epilogue value, stored as it is computed
 #pragma unroll
@@ -396,6 +412,26 @@ __global__ void __launch_bounds__(DeepCfg<BN>::THREADS, 1)
           staging[m * 128 + r] = (uint16_t)h2;
           staging[(m + 1) * 128 + r] = (uint16_t)(h2 >> 16);
         }
+      }
+      if (p.swiglu) {
+        // hidden = bf16(bf16(silu(gate)) * up) of the staged BF16 projections; lane l writes
+        // hidden columns col0 + 2l, 2l + 1 of each of its 16 rows (128 bytes per row), at the
+        // row's route id when grouped launches scatter
+        named_barrier_sync(1, 32 * EPI);
+        for (int mi = 0; mi < EPI_ROWS; ++mi) {
+          const int m = m0 + mi;
+          if (m >= rows_valid) break;
+          const uint32_t gv = *reinterpret_cast<const uint32_t *>(staging + m * 128 + 2 * lane);
+          const uint32_t uv = *reinterpret_cast<const uint32_t *>(staging + m * 128 + 64 + 2 * lane);
+          const float h0 = __fmul_rn(bf16_to_f32(p.silu_tab[gv & 0xffffu]), __uint_as_float(uv << 16));
+          const float h1 = __fmul_rn(bf16_to_f32(p.silu_tab[gv >> 16]), __uint_as_float(uv & 0xffff0000u));
+          uint32_t h2;
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(h1), "f"(h0));
+          const int64_t orow = (GROUPED && p.scatter) ? (int64_t)p.perm[row0 + m] : row0 + m;
+          *reinterpret_cast<uint32_t *>(p.out + orow * p.ldo + col0 + 2 * lane) = h2;
+        }
+        named_barrier_sync(1, 32 * EPI);  // the staging buffer is free for the next tile
+        continue;
       }
       const RowDest dest = fetch_row_dest<GROUPED>(p, row0, rows_valid, m0, m0 + EPI_ROWS, lane);
       named_barrier_sync(1, 32 * EPI);

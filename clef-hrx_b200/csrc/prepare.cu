@@ -122,6 +122,25 @@ __device__ const uint16_t g_silu_bf16[kSiluEntries] __align__(16) = {
 #include "silu_bf16.inc"
 };
 
+// Device address of the table on the current device (looked up once per device), for the
+// GEMM epilogue that applies SwiGLU; null if the lookup fails.
+const uint16_t *silu_table_device() {
+  static std::atomic<const uint16_t *> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  const uint16_t *p = cache[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void *addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_silu_bf16) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    p = static_cast<const uint16_t *>(addr);
+    cache[dev].store(p, std::memory_order_release);
+  }
+  return p;
+}
+
 // KIND_PLAIN and KIND_SILU_TABLE are the GEMM-input paths: int4 codes plus the s8 operand,
 // with no pre-op or with SwiGLU through the table.  KIND_GENERAL reads mode, bits and the
 // operand pointer at run time (SwiGLU evaluated directly, attention gate, RMSNorm).

@@ -228,6 +228,22 @@ CLEFQ_API int clefq_expert(void *stream, const void *a_codes, int64_t a_ld_words
                            int64_t workspace_bytes);
 
 /*
+ * Gate and up experts with SwiGLU in the GEMM epilogue, one launch; replaces the reference's
+ * fused gate/up experts omni_gate_up (src/omni.rs:302-373,
+ * benches/kernels/omni_gate_up_i4.loom):
+ *   out[r][c] = bf16(bf16(silu(g)) * u), g and u the BF16 expert projections of clefq_expert
+ *   (input_routed = 0) by gate_tiled and up_tiled, for route r of groups; out BF16
+ *   [tokens*topk][n], rows in route order.
+ * Each CTA of the pair holds 64 gate and the matching 64 up weight rows, so both operands of
+ * every SwiGLU meet in one accumulator.  Checks: n % 256 == 0, k % 256 == 0, k >= 2048.
+ * workspace >= clefq_expert_workspace_size(tokens, topk, experts, k).
+ */
+CLEFQ_API int clefq_expert_gate_up(void *stream, const void *a_codes, int64_t a_ld_words, const float *a_scales,
+                                   const void *gate_tiled, const float *gate_scales, const void *up_tiled,
+                                   const float *up_scales, const float *groups, int64_t tokens, int topk, int experts,
+                                   int64_t k, int64_t n, void *out, void *workspace, int64_t workspace_bytes);
+
+/*
  * Weighted combine in ascending expert order with BF16 rounding at each step; replaces
  * omni_combine_ordered (order != NULL) and omni_combine (order == NULL)
  * (src/omni.rs:246-278,535-556; kernels/omni_combine{,_ordered}.loom).
@@ -242,6 +258,8 @@ CLEFQ_API int clefq_combine(void *stream, const void *values, const float *route
  * project_swiglu(gate, up, down, residual) (src/backbone.rs:880-894,
  * src/quantized.rs:406-439), bit-identical to those separate steps:
  *   prepare(x) -> gate, up projections -> SwiGLU -> prepare -> down projection (+ residual)
+ * With hidden >= 2048 and inter % 256 == 0 the gate|up launch applies SwiGLU in its epilogue
+ * and writes the hidden rows; otherwise SwiGLU is fused into their packing.
  *   x BF16 [m][hidden]; gate/up tiled [inter][hidden] + scales; down tiled [hidden][inter]
  *   out BF16 [m][hidden]; residual BF16 [m][hidden] or NULL
  * workspace >= clefq_mlp_workspace_size(m, hidden, inter).

@@ -5,8 +5,9 @@ Inputs follow the BASELINE distributions (seeded): activations BF16 N(0, 1); wei
 uniform in [-8, 7] (uniform random tiled words, so -8 occurs, which the reference's packer
 never emits but its GEMM fixture does); one f32 scale per output row |N(0, 0.02)|/7; router
 logits from a BF16 N(0, 1) router weight.  These are the shapes bench.py times, so the
-two-sub-tile dense kernel at K=4096/12288 with its per-tile K rotation and partial last wave,
-and the grouped expert kernels at the C4 per-expert tile counts, are all checked here.
+deep-ring dense kernel at K=4096/12288 with its per-tile K rotation, partial last wave and
+SwiGLU epilogue, and the grouped expert kernels at the C4 per-expert tile counts, are all
+checked here.
 """
 import numpy as np
 import pytest
@@ -155,4 +156,33 @@ def test_c4_moe_layer_full_size(cq):
         assert same_bits_f32(routes_out.cpu().numpy(), ref_routes)
         got = from_dev_bf16(out)
         assert np.array_equal(got, ref), f"{int((got != ref).sum())} of {ref.size} outputs differ"
+    cq.status()
+
+
+@pytest.mark.parametrize("tokens,inter,skewed", [(8192, 768, False), (300, 256, True), (1, 512, False)])
+def test_fused_gate_up_experts(cq, tokens, inter, skewed):
+    """omni_gate_up (src/omni.rs:302-373): gate and up experts with SwiGLU in the GEMM epilogue,
+    against the oracle's two expert projections and SwiGLU, bit for bit (C4 shape first)."""
+    from tests.golden.make_golden import expert_routes
+    rng = np.random.default_rng(tokens + inter)
+    hidden, experts = 2048, 128
+    g, gdev = baseline_weight(cq, rng, experts * inter, hidden)
+    u, udev = baseline_weight(cq, rng, experts * inter, hidden)
+    if tokens == 8192:
+        x = bf16_normal(rng, (tokens, hidden))
+        wr = bf16_normal(rng, (experts, hidden))
+        routes = o.route(o.f32_to_bf16(o.bf16_to_f32(x) @ o.bf16_to_f32(wr).T))
+    else:
+        x = bf16_normal(rng, (tokens, hidden))
+        routes = expert_routes(tokens, skewed, 0)
+    groups, _ = o.group(routes)
+    _, xc, xs, _ = o.prepare(x, 4, o.stride_for(hidden))
+    gate_ref = o.expert(xc, xs, g[0], g[1], groups, tokens, hidden, inter, False)
+    up_ref = o.expert(xc, xs, u[0], u[1], groups, tokens, hidden, inter, False)
+    ref = o.swiglu(gate_ref, up_ref)
+    a = cq.prepare(to_dev_bf16(x), 4, o.stride_for(hidden))
+    for _ in range(2):
+        out = cq.omni_gate_up(a, to_dev(routes), to_dev(groups), gdev, udev)
+        got = from_dev_bf16(out)
+        assert np.array_equal(got, ref), f"{int((got != ref).sum())} of {ref.size} differ"
     cq.status()
