@@ -36,7 +36,9 @@ _SYMBOLS = {
     "clefq_gemm_s8": (ctypes.c_int, ["p", "i", "p", "l", "p", "l", "p", "p", "l", "l", "p", "l", "i", "p", "l"]),
     "clefq_gemm_noalloc": (ctypes.c_int, ["p", "p", "l", "p", "l", "p", "p", "l", "l", "p", "l", "i", "p", "l"]),
     "clefq_gemm_pair_s8": (ctypes.c_int, ["p", "p", "l", "p", "l", "p", "p", "p", "p", "l", "l", "p", "l"]),
+    "clefq_gemm_swiglu_s8": (ctypes.c_int, ["p", "p", "l", "p", "l", "p", "p", "p", "p", "l", "l", "p", "l"]),
     "clefq_swiglu": (ctypes.c_int, ["p", "p", "p", "l", "p"]),
+    "clefq_silu": (ctypes.c_int, ["p", "p", "l", "p"]),
     "clefq_route": (ctypes.c_int, ["p", "p", "i", "l", "i", "i", "p"]),
     "clefq_route_linear": (ctypes.c_int, ["p", "p", "p", "l", "l", "i", "i", "p", "p"]),
     "clefq_group_workspace_size": (ctypes.c_int64, ["l", "i", "i"]),
@@ -273,6 +275,18 @@ def swiglu(gate, up):
     return out
 
 
+def silu(x):
+    """bf16(x / (1 + exp(-x))) of BF16 values, as the SwiGLU GEMM epilogue computes it
+    (clefq_silu)."""
+    _need_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("SiLU takes BF16")
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    _call("clefq_silu", _stream(), _ptr(x), x.numel(), _ptr(out))
+    return out
+
+
 def project_swiglu(gate, up, w: QuantizedWeight, residual=None):
     """src/quantized.rs:406-439: fused SwiGLU packing then the projection."""
     if gate.shape != up.shape or gate.shape[1] != w.cols:
@@ -333,6 +347,21 @@ def project_pair_prepared(rows, w0: QuantizedWeight, w1: QuantizedWeight, a: Pre
         out = torch.empty((rows, 2 * n), dtype=torch.bfloat16, device=a.codes.device)
     _call("clefq_gemm_pair_s8", _stream(), _ptr(a.operand), a.operand.stride(0), _ptr(a.scales), rows,
           _ptr(w0.codes), _ptr(w0.scales), _ptr(w1.codes), _ptr(w1.scales), n, w0.cols, _ptr(out), out.stride(0))
+    return out
+
+
+def project_swiglu_prepared(rows, gate: QuantizedWeight, up: QuantizedWeight, a: Prepared, out=None):
+    """Gate and up projections of one prepared input with SwiGLU in the GEMM epilogue, the
+    gate|up step of the MLP block: returns BF16 [rows][n] = swiglu(x.gate, x.up)
+    (clefq_gemm_swiglu_s8)."""
+    if a.operand is None or a.bits != 4 or gate.rows != up.rows or gate.cols != up.cols:
+        raise ValueError("SwiGLU projection needs an int4 s8 operand and two weights of one shape")
+    n = gate.rows
+    if out is None:
+        out = torch.empty((rows, n), dtype=torch.bfloat16, device=a.codes.device)
+    _call("clefq_gemm_swiglu_s8", _stream(), _ptr(a.operand), a.operand.stride(0), _ptr(a.scales), rows,
+          _ptr(gate.codes), _ptr(gate.scales), _ptr(up.codes), _ptr(up.scales), n, gate.cols, _ptr(out),
+          out.stride(0))
     return out
 
 

@@ -335,12 +335,35 @@ int clefq_gemm_pair_s8(void *stream, const void *operand, int64_t operand_ld, co
                   out_ld);
 }
 
+int clefq_gemm_swiglu_s8(void *stream, const void *operand, int64_t operand_ld, const float *a_scales, int64_t m,
+                         const void *gate_tiled, const float *gate_scales, const void *up_tiled,
+                         const float *up_scales, int64_t n, int64_t k, void *out, int64_t out_ld) {
+  // the GEMM is 2n wide (gate | up); its SwiGLU output is n wide, checked on its own below
+  int rc = check_gemm(4, m, 2 * n, k, operand_ld, nullptr, 0, CLEFQ_BF16, 2 * n);
+  if (rc) return rc;
+  if (!gate_tiled || !up_tiled) return set_err(CLEFQ_ERR_SHAPE, "two weight matrices needed");
+  if (!gemm_swiglu_ok(n, k) || out_ld < n || out_ld % 2)
+    return set_err(CLEFQ_ERR_SHAPE, "SwiGLU epilogue needs n % 256 == 0, k >= 2048 and an even out_ld >= n");
+  if (m == 0) return 0;
+  return run_gemm(static_cast<cudaStream_t>(stream), 4, static_cast<const uint8_t *>(operand), operand_ld, m, a_scales,
+                  m, gate_tiled, gate_scales, up_tiled, up_scales, (int)(n / 128), 2 * n, k, nullptr, 0, CLEFQ_BF16,
+                  out, out_ld, nullptr, 0, true);
+}
+
 int clefq_swiglu(void *stream, const void *gate, const void *up, int64_t n, void *out) {
   if (n < 0) return set_err(CLEFQ_ERR_SHAPE, "SwiGLU shape/dtype mismatch");
   if (n == 0) return 0;
   int rc = launch_swiglu(static_cast<const uint16_t *>(gate), static_cast<const uint16_t *>(up),
                          static_cast<uint16_t *>(out), n, static_cast<cudaStream_t>(stream), device_sms());
   return rc ? cuda_err("swiglu launch") : 0;
+}
+
+int clefq_silu(void *stream, const void *x, int64_t n, void *out) {
+  if (n < 0) return set_err(CLEFQ_ERR_SHAPE, "SiLU element count");
+  if (n == 0) return 0;
+  int rc = launch_silu(static_cast<const uint16_t *>(x), static_cast<uint16_t *>(out), n,
+                       static_cast<cudaStream_t>(stream), device_sms());
+  return rc ? cuda_err("silu launch") : 0;
 }
 
 int clefq_route(void *stream, const void *logits, int logits_dtype, int64_t tokens, int experts, int topk,
@@ -831,8 +854,10 @@ static int run_expert_ffn(cudaStream_t s, const uint8_t *xs, int64_t nroutes, co
   int rc = launch_gemm(p, s);
   if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert gate/up launch") : set_err(rc, "expert gate/up shape");
   // SwiGLU fused into the packing of the hidden rows (still expert-sorted).  The gate|up
-  // launch with SwiGLU in its epilogue (clefq_expert_gate_up) measured 0.641 against 0.564 ms
-  // for the C4 layer: its two 8 KB weight boxes per 192-token stage outrun the TMA unit.
+  // launch with SwiGLU in its epilogue (clefq_expert_gate_up) measured 0.656 against 0.571 ms
+  // for the C4 layer (0.641 against 0.564 with table lookups for SiLU).  The likely cause is
+  // its two 8 KB weight boxes per 192-token stage, one per weight map, where the plain launch
+  // moves one 16 KB box: the TMA unit's rate is per box.
   rc = run_prepare(s, CLEFQ_PREP_SWIGLU, 4, gu, 2 * inter, gu + inter, 2 * inter, nroutes, inter, inter, hq, h8, inter,
                    nullptr, 0, nullptr, nullptr, nullptr, 0, 0, ret ? ret->rows_dev : nullptr);
   if (rc) return rc;

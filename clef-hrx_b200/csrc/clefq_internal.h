@@ -48,6 +48,7 @@ struct PrepareArgs {
 int launch_prepare(const PrepareArgs &a, cudaStream_t stream);
 const uint16_t *silu_table_device();  // the BF16 SiLU table on the current device
 int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);
+int launch_silu(const uint16_t *x, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms);
 int launch_retile(const uint32_t *codes, int64_t rows, int64_t in_words, int64_t words, uint32_t *out,
                   cudaStream_t stream, int num_sms);
 int launch_unpack_i4(const uint32_t *a, int64_t a_ld, int64_t rows, int k, uint8_t *op, int64_t op_ld,

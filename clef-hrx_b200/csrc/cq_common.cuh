@@ -24,6 +24,31 @@ CQ_DEV float minnum(float a, float b) { return fminf(a, b); }
 CQ_DEV uint32_t nib_lo16(uint32_t w) { return (w << 4) & 0xF0F0F0F0u; }
 CQ_DEV uint32_t nib_hi16(uint32_t w) { return w & 0xF0F0F0F0u; }
 
+// SiLU of one BF16 input rounded to BF16, bit-identical to silu_bf16() (cq_math.h) and to the
+// table generated from it (tab, 65,536 entries), without reading the table in the common case.
+// Ziv's rounding test (A. Ziv, "Fast evaluation of elementary mathematical functions with
+// correctly rounded last bit", ACM TOMS 17(3), 1991): for -16 < g < 8 the quotient
+// q = g * rcp(1 + 2^(-g log2(e))) from the hardware's approximate exp2 and reciprocal lies
+// within about 40 units of 2^-24 (relative) of the reference quotient g / (1 + exp_cw(-g)):
+// the product g log2(e) carries at most |g log2(e)| 2^-24 of absolute error (about 24 units
+// through 2^x), exp2 and the reciprocal a few units each, the reference a few more.  When q's
+// bits lie more than kSiluMargin f32 steps from a BF16 rounding midpoint, both quotients round
+// to the same BF16 value.  g >= 8 (and +Inf) gives g exactly; the rest (g <= -16, -Inf, NaN)
+// and the near-midpoint cases (about 0.4% of inputs) read the table.  The exhaustive GPU test
+// of clefq_silu checks every BF16 input against the table.
+constexpr uint32_t kSiluMargin = 128;
+CQ_DEV uint32_t silu_bf16_ziv(uint32_t g16, const uint16_t *__restrict__ tab) {
+  const float g = __uint_as_float(g16 << 16);
+  float t, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(__fmul_rn(g, -1.44269502162933349609375f)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, t)));
+  const uint32_t b = __float_as_uint(__fmul_rn(g, r));
+  uint32_t out = (b + 0x7fffu + ((b >> 16) & 1u)) >> 16;  // nearest even; q is finite here
+  const bool fast = g > -16.0f && g < 8.0f && ((b + (kSiluMargin - 0x8000u)) & 0xffffu) > 2 * kSiluMargin;
+  if (!fast) out = g >= 8.0f ? g16 : (uint32_t)__ldg(tab + g16);
+  return out;
+}
+
 // ---------------------------------------------------------------------------------------
 // Shared-memory addresses, mbarriers, TMA, tcgen05 (inline PTX for sm_100a)
 // ---------------------------------------------------------------------------------------

@@ -364,6 +364,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 #include "gemm2sm.cuh"
 #include "gemm2sm_deep.cuh"
+#ifndef CLEFQ_DEEP_MIN_KSTAGES
+#define CLEFQ_DEEP_MIN_KSTAGES 8   // fewest 256-wide K stages an int4 launch needs for the deep-ring kernel
+#endif
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -561,7 +564,7 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
     // and 192 for grouped ones (their tile lists are built for 192 rows).  Shorter K keeps
     // the two-stage kernel, whose double-buffered accumulators hide the tile hand-over that
     // a few K stages cannot amortise.
-    const bool deep = p.bits == 4 && p.k / 256 >= 8;
+    const bool deep = p.bits == 4 && p.k / 256 >= CLEFQ_DEEP_MIN_KSTAGES;
 #else
     const bool deep = false;
 #endif

@@ -414,17 +414,21 @@ __global__ void __launch_bounds__(DeepCfg<BN>::THREADS, 1)
         }
       }
       if (p.swiglu) {
-        // hidden = bf16(bf16(silu(gate)) * up) of the staged BF16 projections; lane l writes
+        // hidden = bf16(bf16(silu(gate)) * up) of the staged BF16 projections (SiLU by
+        // silu_bf16_ziv: arithmetic, the table only near rounding midpoints); lane l writes
         // hidden columns col0 + 2l, 2l + 1 of each of its 16 rows (128 bytes per row), at the
         // row's route id when grouped launches scatter
         named_barrier_sync(1, 32 * EPI);
+#pragma unroll 2
         for (int mi = 0; mi < EPI_ROWS; ++mi) {
           const int m = m0 + mi;
           if (m >= rows_valid) break;
           const uint32_t gv = *reinterpret_cast<const uint32_t *>(staging + m * 128 + 2 * lane);
           const uint32_t uv = *reinterpret_cast<const uint32_t *>(staging + m * 128 + 64 + 2 * lane);
-          const float h0 = __fmul_rn(bf16_to_f32(p.silu_tab[gv & 0xffffu]), __uint_as_float(uv << 16));
-          const float h1 = __fmul_rn(bf16_to_f32(p.silu_tab[gv >> 16]), __uint_as_float(uv & 0xffff0000u));
+          const uint32_t s0 = silu_bf16_ziv(gv & 0xffffu, p.silu_tab);
+          const uint32_t s1 = silu_bf16_ziv(gv >> 16, p.silu_tab);
+          const float h0 = __fmul_rn(__uint_as_float(s0 << 16), __uint_as_float(uv << 16));
+          const float h1 = __fmul_rn(__uint_as_float(s1 << 16), __uint_as_float(uv & 0xffff0000u));
           uint32_t h2;
           asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(h1), "f"(h0));
           const int64_t orow = (GROUPED && p.scatter) ? (int64_t)p.perm[row0 + m] : row0 + m;

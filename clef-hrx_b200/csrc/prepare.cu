@@ -885,6 +885,21 @@ __global__ void swiglu_tail_kernel(const uint16_t *g, const uint16_t *u, uint16_
   }
 }
 
+// SiLU of n BF16 values as the SwiGLU GEMM epilogue computes it (silu_bf16_ziv).
+__global__ void silu_kernel(const uint16_t *__restrict__ x, uint16_t *__restrict__ out, int64_t n,
+                            const uint16_t *__restrict__ tab) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = (uint16_t)silu_bf16_ziv(x[i], tab);
+}
+
+int launch_silu(const uint16_t *x, uint16_t *out, int64_t n, cudaStream_t stream, int num_sms) {
+  const uint16_t *tab = silu_table_device();
+  if (!tab) return (int)cudaErrorInvalidSymbol;
+  const int64_t blocks = (n + 255) / 256, cap = (int64_t)num_sms * 8;
+  silu_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(x, out, n, tab);
+  return launch_check();
+}
+
 int launch_swiglu(const uint16_t *g, const uint16_t *u, uint16_t *out, int64_t n, cudaStream_t stream,
                   int num_sms) {
   const int64_t n8 = n / 8;

@@ -168,9 +168,23 @@ CLEFQ_API int clefq_gemm_pair_s8(void *stream, const void *operand, int64_t oper
                                  int64_t m, const void *w0_tiled, const float *w0_scales, const void *w1_tiled,
                                  const float *w1_scales, int64_t n, int64_t k, void *out, int64_t out_ld);
 
+/*
+ * Gate and up of one packed int4 input in one launch with SwiGLU in the epilogue, the gate|up
+ * step of clefq_mlp: out BF16 [m][n] = bf16(bf16(silu(g)) * u) with g, u the BF16 projections
+ * x.gate and x.up, bit-identical to project_quantized by gate and by up, then swiglu (src/quantized.rs:235-253,
+ * src/ops.rs:9-29).  Checks: n % 256 == 0, k % 256 == 0, k >= 2048, out_ld even and >= n.
+ */
+CLEFQ_API int clefq_gemm_swiglu_s8(void *stream, const void *operand, int64_t operand_ld, const float *a_scales,
+                                   int64_t m, const void *gate_tiled, const float *gate_scales, const void *up_tiled,
+                                   const float *up_scales, int64_t n, int64_t k, void *out, int64_t out_ld);
+
 /* SwiGLU bf16(bf16(g/(1+exp(-g))) * u); replaces Engine::swiglu (src/ops.rs:9-29,
  * kernels/swiglu.loom:41-50).  n elements, BF16. */
 CLEFQ_API int clefq_swiglu(void *stream, const void *gate, const void *up, int64_t n, void *out);
+
+/* SiLU bf16(g/(1+exp(-g))) of n BF16 values, the activation half of SwiGLU
+ * (kernels/swiglu.loom:41-50), computed exactly as the SwiGLU GEMM epilogue computes it. */
+CLEFQ_API int clefq_silu(void *stream, const void *x, int64_t n, void *out);
 
 /*
  * Router; replaces omni_route (src/omni.rs:170-190, kernels/omni_route.loom:84-147):
@@ -273,8 +287,8 @@ CLEFQ_API int clefq_mlp(void *stream, const void *x, int64_t m, int64_t hidden, 
  * Pre-norm MLP block with the input as residual; replaces normalized_mlp
  * (src/quantized.rs:348-404): RMSNorm (weight + 1 offset, eps 1e-6, mean over `hidden`)
  * fused into the packing of x (prepare_norm_with_source, src/quantized.rs:615-640), gate and
- * up projections of the shared codes, SwiGLU fused into the packing of the hidden rows, and
- * the down projection with x itself as residual:
+ * up projections of the shared codes, SwiGLU (in the gate|up epilogue or the packing of the
+ * hidden rows, as clefq_mlp chooses), and the down projection with x itself as residual:
  *   out = bf16(x + bf16(down(swiglu(gate(norm(x)), up(norm(x))))))
  * norm_weight BF16 [hidden].  out may be x (each element is read before it is overwritten).
  * The reference takes this path only at width 5120 and 17408 intermediate rows; any width

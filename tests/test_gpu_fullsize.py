@@ -71,9 +71,9 @@ def test_c2_mlp_block_full_size(cq):
 
 
 def test_c2_gate_up_pair_and_down_full_size(cq):
-    """C2's two GEMM launches as clefq_mlp issues them: gate|up as one paired launch
-    (N = 2 x 12288, two weight maps) and the down projection (K = 12288) with F32 output and
-    with a BF16 residual."""
+    """C2's GEMM launches: gate|up as one paired launch (N = 2 x 12288, two weight maps), plain
+    and with SwiGLU in the epilogue as clefq_mlp issues it, and the down projection (K = 12288)
+    with F32 output and with a BF16 residual."""
     rng = np.random.default_rng(3)
     m, h, inter = 4096, 4096, 12288
     g, gdev = baseline_weight(cq, rng, inter, h)
@@ -82,8 +82,13 @@ def test_c2_gate_up_pair_and_down_full_size(cq):
     _, codes, scales, _ = o.prepare(x, 4, o.stride_for(h))
     a = cq.prepare(to_dev_bf16(x), 4, o.stride_for(h))
     pair = from_dev_bf16(cq.project_pair_prepared(m, gdev, udev, a))
-    assert np.array_equal(pair[:, :inter], o.gemm(codes, scales, g[0], g[1], inter, h))
-    assert np.array_equal(pair[:, inter:], o.gemm(codes, scales, u[0], u[1], inter, h))
+    gate_ref = o.gemm(codes, scales, g[0], g[1], inter, h)
+    up_ref = o.gemm(codes, scales, u[0], u[1], inter, h)
+    assert np.array_equal(pair[:, :inter], gate_ref)
+    assert np.array_equal(pair[:, inter:], up_ref)
+    # the same launch with SwiGLU in its epilogue, as clefq_mlp issues it at this shape
+    fused = from_dev_bf16(cq.project_swiglu_prepared(m, gdev, udev, a))
+    assert np.array_equal(fused, o.swiglu(gate_ref, up_ref))
 
     d, ddev = baseline_weight(cq, rng, h, inter)
     hid = bf16_normal(rng, (m, inter))

@@ -249,11 +249,62 @@ def test_gemm_residual(cq, m):
     assert np.array_equal(got[~nan_ref], ref[~nan_ref])
 
 
-def test_mlp_block(cq):
+def test_silu_every_bf16_input(cq):
+    """The SwiGLU epilogue's SiLU (approximate exp2 and reciprocal with Ziv's rounding test,
+    the table near BF16 rounding midpoints) equals the reference SiLU on all 65,536 BF16 bit
+    patterns, NaN payloads included (oracle: swiglu with up = 1, exact for every value)."""
+    g = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    ones = np.full(65536, 0x3F80, dtype=np.uint16)
+    ref = o.swiglu(g, ones)
+    got = from_dev_bf16(cq.silu(to_dev_bf16(g)))
+    bad = np.nonzero(got != ref)[0]
+    assert bad.size == 0, [(hex(int(i)), hex(int(got[i])), hex(int(ref[i]))) for i in bad[:8]]
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 256, 2048), (130, 512, 2048), (513, 256, 4096), (77, 768, 6144)])
+def test_gemm_swiglu_epilogue(cq, m, n, k):
+    """Gate|up in one launch with SwiGLU in the epilogue (clefq_gemm_swiglu_s8, the gate|up step
+    of clefq_mlp) equals swiglu of the two oracle projections, bit for bit.  Row 0 is scaled so
+    that its projections reach the dense epilogue's finite BF16 clamp and the SwiGLU products
+    overflow; NaN positions, if any, must agree."""
+    rng = np.random.default_rng(m + n + k)
+    _, gt, gs, gdev = _weight(rng, n, k)
+    _, ut, us, udev = _weight(rng, n, k)
+    x = bf16_normal(rng, (m, k))
+    x[0, :] = o.f32_to_bf16(np.full(k, 1e34, np.float32))
+    stride = o.stride_for(k)
+    _, ocodes, oscales, _ = o.prepare(x, 4, stride)
+    ref = o.swiglu(o.gemm(ocodes, oscales, gt, gs, n, k), o.gemm(ocodes, oscales, ut, us, n, k))
+    a = cq.prepare(to_dev_bf16(x), 4, stride)
+    nan_ref = np.isnan(o.bf16_to_f32(ref))
+    for _ in range(2):
+        got = from_dev_bf16(cq.project_swiglu_prepared(m, gdev, udev, a))
+        assert np.array_equal(np.isnan(o.bf16_to_f32(got)), nan_ref)
+        assert np.array_equal(got[~nan_ref], ref[~nan_ref])
+    # a wider output row (out_ld > n) leaves the padding untouched
+    wide = torch.full((m, n + 256), -1.0, dtype=torch.bfloat16, device="cuda")
+    cq.project_swiglu_prepared(m, gdev, udev, a, out=wide[:, :n])
+    got = from_dev_bf16(wide)
+    assert np.array_equal(got[:, :n][~nan_ref], ref[~nan_ref])
+    assert np.all(got[:, n:] == o.f32_to_bf16(np.float32(-1.0)))
+
+
+def test_gemm_swiglu_rejects_unsupported_shapes(cq):
+    rng = np.random.default_rng(3)
+    for n, k in ((128, 2048), (256, 1024)):       # n % 256, K below the deep kernel's range
+        _, _, _, gdev = _weight(rng, n, k)
+        _, _, _, udev = _weight(rng, n, k)
+        a = cq.prepare(to_dev_bf16(bf16_normal(rng, (4, k))), 4, o.stride_for(k))
+        with pytest.raises(ValueError):
+            cq.project_swiglu_prepared(4, gdev, udev, a)
+
+
+@pytest.mark.parametrize("m,h,inter", [(200, 1024, 768), (300, 2048, 768), (1, 2048, 256), (257, 4096, 1280)])
+def test_mlp_block(cq, m, h, inter):
     """Dense SwiGLU MLP block through one C-ABI call, bit-exact to the oracle's separate
-    steps (prepare, gate, up, swiglu, prepare, down)."""
-    rng = np.random.default_rng(5)
-    m, h, inter = 200, 1024, 768
+    steps (prepare, gate, up, swiglu, prepare, down); hidden 1024 and inter 1280 take the
+    SwiGLU-in-packing route, the others SwiGLU in the gate|up epilogue."""
+    rng = np.random.default_rng(5 + m)
     ws = []
     for n, k in ((inter, h), (inter, h), (h, inter)):
         _, wt, s, dev = _weight(rng, n, k)
