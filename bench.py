@@ -608,6 +608,7 @@ def run_clefq(args, world, rank, local):
                           dtype=torch.uint8, device="cuda")
         nccl_ms = None
         parity = None
+        parity_paths = None
         if world > 1:
             # expert parallel: this rank owns MOE_E / world experts and its own MOE_T tokens;
             # one clefq_moe_ep_layer call per step (records and products stored into the peers'
@@ -624,14 +625,22 @@ def run_clefq(args, world, rank, local):
             # parity before timing: both expert-parallel paths against clefq_moe on one GPU
             ref = clefq.omni_moe(mx, logits, mg, mu, md, workspace=mws)
             nccl_out = nstep()[0]
-            omni_moe_ep_fused(mx, None, shard, ecomm, MOE_K, recv_cap=cap, workspace=ews, out=eout, router_weight=wr)
-            ref_fused = clefq.omni_moe(mx, None, mg, mu, md, workspace=mws, router_weight=wr)
+            # the fused layer from the precomputed logits, then with the router linear fused in
+            lout, _ = omni_moe_ep_fused(mx, logits, shard, ecomm, MOE_K, recv_cap=cap, workspace=ews)
+            _, eroutes = omni_moe_ep_fused(mx, None, shard, ecomm, MOE_K, recv_cap=cap, workspace=ews, out=eout,
+                                           router_weight=wr)
+            rroutes = torch.empty((MOE_T, 2 * MOE_K), dtype=torch.float32, device="cuda")
+            ref_fused = clefq.omni_moe(mx, None, mg, mu, md, workspace=mws, router_weight=wr, routes_out=rroutes)
             torch.cuda.synchronize()
             clefq.status()
-            same = torch.equal(eout.view(torch.int16), ref_fused.view(torch.int16)) and \
-                torch.equal(nccl_out.view(torch.int16), ref.view(torch.int16))
-            parity = all_min(world, same)
-            del ref, nccl_out, ref_fused
+            same_fused = torch.equal(eout.view(torch.int16), ref_fused.view(torch.int16))
+            same_nccl = torch.equal(nccl_out.view(torch.int16), ref.view(torch.int16))
+            parity = all_min(world, same_fused and same_nccl)
+            parity_paths = {"fused": all_min(world, same_fused), "nccl": all_min(world, same_nccl),
+                            "fused_routes": all_min(world, torch.equal(eroutes, rroutes)),
+                            "fused_from_logits": all_min(world, torch.equal(lout.view(torch.int16),
+                                                                            ref.view(torch.int16)))}
+            del ref, nccl_out, ref_fused, lout, eroutes, rroutes
             for _ in range(3):
                 nstep()
             torch.cuda.synchronize()
@@ -673,7 +682,7 @@ def run_clefq(args, world, rank, local):
                               "stored into peers' buffers over NVLink by the kernels" if world > 1
                else "single GPU", "tokens_per_s": world * MOE_T / (mms / 1000), "ms_per_step": mms,
                "nccl_all_to_all_ms_per_step": nccl_ms,
-               "parity": parity,
+               "parity": parity, "parity_paths": parity_paths,
                "router": "router linear fused with the router (clefq_route_linear's kernel) inside the timed "
                          "layer; the NCCL composition routes from precomputed logits",
                "parity_note": "each rank's fused and NCCL expert-parallel outputs equal clefq_moe over the same "

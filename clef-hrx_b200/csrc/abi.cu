@@ -808,21 +808,14 @@ void *clefq_tp_mlp_output(clefq_comm *c, int64_t m, int64_t hidden, int64_t inte
 // ---- grouped expert FFN shared by the fused MoE block and the expert-parallel path ----
 // xs: expert-sorted s8 operand rows (route order given by perm); a_scales: the token
 // scale of route r at a_scales[r / topk].  Writes values[route] = down(SwiGLU(gate|up)).
-// Expert-parallel variant: nroutes is the capacity, rows_dev the routes present (on the
-// device), and `ret` sends each route's bf16(value * probability) to its home rank.
-struct ExpertReturn {
-  const int64_t *rows_dev;
-  uint16_t *base[kMaxRanks];
-  const int *rank, *row;
-  const float *prob;
-};
-
+// Expert-parallel variant: nroutes is the capacity and rows_dev the routes present (a
+// count on the device).
 static int run_expert_ffn(cudaStream_t s, const uint8_t *xs, int64_t nroutes, const float *a_scales, int topk,
                           const int *tiles, const int *offsets, const int *perm, int experts, int tile_rows,
                           int64_t hidden, int64_t inter, const void *gate_tiled, const float *gate_scales,
                           const void *up_tiled, const float *up_scales, const void *down_tiled,
                           const float *down_scales, uint16_t *gu, uint32_t *hq, uint8_t *h8, uint16_t *values,
-                          const ExpertReturn *ret = nullptr) {
+                          const int64_t *rows_dev = nullptr) {
   int *status = device_status_word();
   if (!status) return cuda_err("status word");
   GemmParams p{};
@@ -859,7 +852,7 @@ static int run_expert_ffn(cudaStream_t s, const uint8_t *xs, int64_t nroutes, co
   // its two 8 KB weight boxes per 192-token stage, one per weight map, where the plain launch
   // moves one 16 KB box: the TMA unit's rate is per box.
   rc = run_prepare(s, CLEFQ_PREP_SWIGLU, 4, gu, 2 * inter, gu + inter, 2 * inter, nroutes, inter, inter, hq, h8, inter,
-                   nullptr, 0, nullptr, nullptr, nullptr, 0, 0, ret ? ret->rows_dev : nullptr);
+                   nullptr, 0, nullptr, nullptr, nullptr, 0, 0, rows_dev);
   if (rc) return rc;
   p.a_op = h8;
   p.a_ld = inter;
@@ -875,12 +868,6 @@ static int run_expert_ffn(cudaStream_t s, const uint8_t *xs, int64_t nroutes, co
   p.ldo = hidden;
   p.scale_mode = 0;  // hidden rows were packed in sorted order
   p.scatter = 1;     // values land at their route id
-  if (ret) {
-    for (int g = 0; g < kMaxRanks; ++g) p.ret_base[g] = ret->base[g];
-    p.ret_rank = ret->rank;
-    p.ret_row = ret->row;
-    p.ret_prob = ret->prob;
-  }
   rc = launch_gemm(p, s);
   if (rc) return rc == CLEFQ_ERR_CUDA ? cuda_err("expert down launch") : set_err(rc, "expert down shape");
   return 0;
@@ -1121,6 +1108,7 @@ struct EpLayerTables {
   int64_t *n_dev;
   uint8_t *xs, *h8;
   uint16_t *gu;
+  uint16_t *vals;  // down-projection values [cap][hidden], over xs and gu (dead by then)
 };
 
 static Arena ep_layer_tables(Arena a, int64_t tokens, int64_t hidden, int64_t inter, int experts, int topk, int world,
@@ -1143,6 +1131,10 @@ static Arena ep_layer_tables(Arena a, int64_t tokens, int64_t hidden, int64_t in
   t.perm = a.take<int>(rows);
   t.xs = a.take<uint8_t>(rows * hidden);
   t.gu = a.take<uint16_t>(rows * 2 * inter);
+  // xs and gu are contiguous (both sizes are multiples of 256 bytes); the values need
+  // rows * hidden * 2 bytes from xs on, so extend the span when 4 * inter < hidden
+  if (hidden > 4 * inter) a.take<uint8_t>(rows * (hidden - 4 * inter));
+  t.vals = reinterpret_cast<uint16_t *>(t.xs);
   t.hq = a.take<uint32_t>(rows * (inter / 8 + 1));
   t.h8 = a.take<uint8_t>(rows * inter);
   return a;
@@ -1293,19 +1285,25 @@ int clefq_moe_ep_layer(clefq_comm *c, void *stream, const void *x, const void *l
   if (recv_cap > 0 && launch_gather_unpack_i4(recv, rec_words, t.perm, 1, recv_cap, (int)hidden, t.xs, hidden, s, sms,
                                               t.n_dev))
     return cuda_err("expert-parallel gather launch");
-  // 5. expert FFN; the down-GEMM epilogue stores bf16(value * probability) at the home
-  //    rank's product row
+  // 5. expert FFN with the values in received-route order, then each product goes home:
+  //    bf16(value * probability) into the home rank's product row, by its own kernel.  (A
+  //    return stored from the down GEMM's epilogue produced wrong tiles at full size -- C4,
+  //    8192 tokens -- also on one rank with local stores only; it was taken out.)
   if (recv_cap > 0) {
-    ExpertReturn ret{};
-    ret.rows_dev = t.n_dev;
-    for (int g = 0; g < world; ++g) ret.base[g] = reinterpret_cast<uint16_t *>(at(g, products));
-    ret.rank = t.ret_rank;
-    ret.row = t.ret_row;
-    ret.prob = t.ret_prob;
     rc = run_expert_ffn(s, t.xs, recv_cap, t.xs_scales, 1, t.tiles, t.offsets, t.perm, local, tile_rows, hidden,
                         inter, gate_tiled, gate_scales, up_tiled, up_scales, down_tiled, down_scales, t.gu, t.hq,
-                        t.h8, nullptr, &ret);
+                        t.h8, t.vals, t.n_dev);
     if (rc) return rc;
+    EpReturnArgs ra{};
+    ra.values = t.vals;
+    ra.n_dev = t.n_dev;
+    ra.cap = recv_cap;
+    ra.hidden = (int)hidden;
+    ra.rank = t.ret_rank;
+    ra.row = t.ret_row;
+    ra.prob = t.ret_prob;
+    for (int g = 0; g < world; ++g) ra.base[g] = reinterpret_cast<uint16_t *>(at(g, products));
+    if (launch_ep_return(ra, s, sms)) return cuda_err("expert-parallel return launch");
   }
   // 6. barrier: every product is home; the reference's ascending-expert chain
   if ((rc = launch_comm_barrier(comm_barrier_args(c, status), s))) return rc;

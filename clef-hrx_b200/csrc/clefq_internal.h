@@ -88,13 +88,6 @@ struct GemmParams {
   // as from out), e.g. peers' symmetric buffers over NVLink
   uint16_t *out_peer[kMaxPeers];
   int n_out_peer;
-  // grouped 2-SM kernel only, expert-parallel return: output row r (a received route) is
-  // stored as bf16(value * ret_prob[r]) at ret_base[ret_rank[r]] + ret_row[r] * ldo (its
-  // home rank's product buffer, over NVLink for a peer) instead of at out
-  uint16_t *ret_base[kMaxRanks];
-  const int *ret_rank;
-  const int *ret_row;
-  const float *ret_prob;
   int store16;              // set by launch_gemm: every output address allows 16-byte stores
   // SwiGLU epilogue (int4, two weight maps: gate in w[0], up in w[1]; deep-ring kernel only):
   // each CTA computes 64 gate and the matching 64 up rows of one hidden-column slab and stores
@@ -208,6 +201,18 @@ struct EpReceiveArgs {
   int *err;
 };
 int launch_ep_dispatch(const EpDispatchArgs &a, cudaStream_t stream, int num_sms);
+// Expert-parallel return: product row p (p < *n_dev) of values [cap][hidden] goes home as
+// bf16(value * prob[p]) to base[rank[p]] + row[p] * hidden (a peer's buffer over NVLink).
+struct EpReturnArgs {
+  const uint16_t *values;
+  const int64_t *n_dev;
+  int64_t cap;
+  int hidden;
+  const int *rank, *row;
+  const float *prob;
+  uint16_t *base[kMaxRanks];
+};
+int launch_ep_return(const EpReturnArgs &a, cudaStream_t stream, int num_sms);
 int launch_ep_receive(const EpReceiveArgs &a, cudaStream_t stream, int num_sms);
 
 int device_sms();

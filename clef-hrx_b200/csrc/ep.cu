@@ -220,6 +220,9 @@ __global__ void ep_dispatch_kernel(EpDispatchArgs a) {
           make_uint4(__float_as_uint(a.scales[t]), (uint32_t)e,
                      __float_as_uint(a.routes[t * 2 * a.topk + a.topk + r]), (uint32_t)i);
   }
+  // every thread makes its own stores into peers visible at system scope before the kernel
+  // ends; the barrier kernel's single-thread fence does not cover other threads' stores
+  __threadfence_system();
 }
 
 // Received records -> per-record activation scale, (local expert, probability) route rows,
@@ -253,6 +256,38 @@ __global__ void ep_receive_kernel(EpReceiveArgs a) {
     a.ret_rank[p] = src;
     a.ret_row[p] = (int)meta.w;
   }
+}
+
+// One warp per received route: its product row goes home scaled by the route's probability,
+// bf16(value * prob), the same rounding as the single-GPU combine's product; 16-byte loads
+// and stores, eight columns per lane and step.
+__global__ void ep_return_kernel(EpReturnArgs a) {
+  const int64_t d = *a.n_dev;
+  const int64_t n = d < 0 ? 0 : (d < a.cap ? d : a.cap);
+  const int lane = threadIdx.x & 31;
+  const int chunks = a.hidden / 8;
+  const int64_t wstride = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t p = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); p < n; p += wstride) {
+    const float pr = a.prob[p];
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.values + p * a.hidden);
+    uint4 *dst = reinterpret_cast<uint4 *>(a.base[a.rank[p]] + (int64_t)a.row[p] * a.hidden);
+    for (int c = lane; c < chunks; c += 32) {
+      uint4 v = __ldcs(src + c);
+      uint16_t *h = reinterpret_cast<uint16_t *>(&v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) h[q] = f32_to_bf16(__fmul_rn(bf16_to_f32(h[q]), pr));
+      dst[c] = v;
+    }
+  }
+  // stores into peers are made visible at system scope before the kernel ends
+  __threadfence_system();
+}
+
+int launch_ep_return(const EpReturnArgs &a, cudaStream_t stream, int num_sms) {
+  if (a.cap <= 0) return 0;
+  int64_t blocks = (a.cap + 7) / 8, cap = (int64_t)num_sms * 16;
+  ep_return_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(a);
+  return launch_check();
 }
 
 int launch_ep_dispatch(const EpDispatchArgs &a, cudaStream_t stream, int num_sms) {

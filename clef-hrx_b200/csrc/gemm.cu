@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_arrive(&s.wsm_empty[st]);
         }
         tmem_st_x32(tmem + lane_base + WCOL0 + 32 * st, o);
-        tmem_st_wait();
+        tmem_st_wait(o);
         tc_fence_before();
         mbar_arrive(&s.wtm_full[st]);
       }
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             my_scale = p.a_scales[pos];
           }
         }
-        tmem_ld_wait();
+        tmem_ld_wait(accv);
         if (c + 32 >= BN) {
           tc_fence_before();
           mbar_arrive(&s.acc_empty[buf]);  // accumulator free for tile i + 2
@@ -510,9 +510,6 @@ static bool allows_store16(const GemmParams &p) {
   if (p.ldo % 8 || (p.out && !al(p.out)) || (p.residual && (!al(p.residual) || p.ldr % 8))) return false;
   for (int d = 0; d < p.n_out_peer; ++d)
     if (!al(p.out_peer[d])) return false;
-  if (p.ret_row)
-    for (int g = 0; g < kMaxRanks; ++g)
-      if (!al(p.ret_base[g])) return false;
   return true;
 }
 
@@ -530,7 +527,6 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
   if (p.residual && ((uintptr_t)p.residual % 8 || p.ldr % 4)) return CLEFQ_ERR_ALIGN;
   const bool pairs = gemm_uses_pairs(p);
   if (p.n_out_peer && (!pairs || p.grouped || !p.out || p.n_out_peer > kMaxPeers)) return CLEFQ_ERR_SHAPE;
-  if (p.ret_row && (!pairs || !p.grouped || !p.scatter || !p.ret_rank || !p.ret_prob)) return CLEFQ_ERR_SHAPE;
   if (p.swiglu && (!pairs || p.bits != 4)) return CLEFQ_ERR_SHAPE;
   for (int d = 0; d < p.n_out_peer; ++d)
     if ((uintptr_t)p.out_peer[d] % 8) return CLEFQ_ERR_ALIGN;
@@ -581,7 +577,7 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
       return CLEFQ_ERR_CUDA;
     if (p.swiglu) {
       // the SwiGLU epilogue pairs gate and up rows of the same hidden columns in one CTA
-      if (!deep || !two || p.residual || p.out_f32 || p.n_out_peer || p.ret_row || (p.scatter && !p.grouped) ||
+      if (!deep || !two || p.residual || p.out_f32 || p.n_out_peer || (p.scatter && !p.grouped) ||
           !p.out || !p.silu_tab || p.ldo % 2)
         return CLEFQ_ERR_SHAPE;
       if (!weight_map_half(enc, &wmap0, p.w[0], wrows, p.k) || !weight_map_half(enc, &wmap1, p.w[1], wrows, p.k))

@@ -94,11 +94,9 @@ template <> struct StoreVec<8> { using T = uint4; };
 
 // Where the rows a warp stores go (grouped mode), read before the tile's accumulator is
 // ready so the loads overlap the mainloop instead of sitting in front of every row store:
-// lane l holds row m_begin + l's output row (perm) and, for the expert-parallel return,
-// that route's probability, home rank and home row.
+// lane l holds row m_begin + l's output row (perm).
 struct RowDest {
-  int orow = 0, rank = 0, rrow = 0;
-  float prob = 0.0f;
+  int orow = 0;
 };
 
 template <bool GROUPED>
@@ -108,11 +106,6 @@ CQ_DEV RowDest fetch_row_dest(const GemmParams &p, int64_t row0, int rows_valid,
   if (GROUPED && m < m_end && m < rows_valid) {
     const int64_t pos = row0 + m;
     d.orow = p.scatter ? p.perm[pos] : (int)pos;
-    if (p.ret_row) {
-      d.prob = p.ret_prob[d.orow];
-      d.rank = p.ret_rank[d.orow];
-      d.rrow = p.ret_row[d.orow];
-    }
   }
   return d;
 }
@@ -120,8 +113,7 @@ CQ_DEV RowDest fetch_row_dest(const GemmParams &p, int64_t row0, int rows_valid,
 // Stores token rows [m_begin, m_end) (at most 32) of a CTA's staged BF16 tile (128 columns
 // from col0): V columns per lane, so 128 / V lanes per row (V = 8: 16-byte stores, two rows
 // per warp instruction).  Dense: optional residual bf16(res + y), and copies to out_peer.
-// Grouped: row scatter through perm, or the expert-parallel return bf16(value * probability)
-// into the route's home rank, with the destinations taken from dest (fetch_row_dest).
+// Grouped: row scatter through perm, with the destinations taken from dest (fetch_row_dest).
 template <bool GROUPED, int V>
 CQ_DEV void store_tile_rows(const GemmParams &p, const uint16_t *staging, int64_t row0, int rows_valid, int col0,
                             int m_begin, int m_end, int lane, const RowDest &dest) {
@@ -134,15 +126,8 @@ CQ_DEV void store_tile_rows(const GemmParams &p, const uint16_t *staging, int64_
     const int mi = it * RPI + sub;  // row within [m_begin, m_end)
     const int m = m_begin + mi;
     int64_t orow = row0 + m;
-    float pr = 0.0f;
-    int rk = 0, rrow = 0;
-    if (GROUPED) {
-      // shuffles run on every lane (mi < 32), before the row checks
-      orow = __shfl_sync(0xffffffffu, dest.orow, mi & 31);
-      pr = __shfl_sync(0xffffffffu, dest.prob, mi & 31);
-      rk = __shfl_sync(0xffffffffu, dest.rank, mi & 31);
-      rrow = __shfl_sync(0xffffffffu, dest.rrow, mi & 31);
-    }
+    // the shuffle runs on every lane (mi < 32), before the row checks
+    if (GROUPED) orow = __shfl_sync(0xffffffffu, dest.orow, mi & 31);
     if (m >= m_end || m >= rows_valid) continue;
     const int64_t pos = row0 + m;
     Vec v = *reinterpret_cast<const Vec *>(staging + m * 128 + V * l);
@@ -152,13 +137,6 @@ CQ_DEV void store_tile_rows(const GemmParams &p, const uint16_t *staging, int64_
       const uint16_t *hr = reinterpret_cast<const uint16_t *>(&rv);
 #pragma unroll
       for (int q = 0; q < V; ++q) hv[q] = f32_to_bf16(__fadd_rn(bf16_to_f32(hr[q]), bf16_to_f32(hv[q])));
-    }
-    if (GROUPED && p.ret_row) {
-#pragma unroll
-      for (int q = 0; q < V; ++q) hv[q] = f32_to_bf16(__fmul_rn(bf16_to_f32(hv[q]), pr));
-      uint16_t *dst = p.ret_base[rk] + (int64_t)rrow * p.ldo + col0 + V * l;
-      *reinterpret_cast<Vec *>(dst) = v;
-      continue;
     }
     const int64_t off = orow * p.ldo + col0 + V * l;
     *reinterpret_cast<Vec *>(p.out + off) = v;
@@ -355,24 +333,27 @@ __global__ void __launch_bounds__(THREADS2, 1)
         tc_fence_after();
         if (BITS == 4) {
           // 8 words per 32-code group -> low nibbles then high nibbles (x16)
+          uint32_t o[2][32];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            uint32_t o[32];
 #pragma unroll
             for (int gq = 0; gq < 4; ++gq) {
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                o[8 * gq + q] = nib_lo16(w[16 * h + 4 * gq + q]);
-                o[8 * gq + 4 + q] = nib_hi16(w[16 * h + 4 * gq + q]);
+                o[h][8 * gq + q] = nib_lo16(w[16 * h + 4 * gq + q]);
+                o[h][8 * gq + 4 + q] = nib_hi16(w[16 * h + 4 * gq + q]);
               }
             }
-            tmem_st_x32(tmem + lane_base + WCOL + 64 * sw + 32 * h, o);
+            tmem_st_x32(tmem + lane_base + WCOL + 64 * sw + 32 * h, o[h]);
           }
+          tmem_st_wait(o[0]);
+          tmem_st_keep(o[1]);
         } else {
           tmem_st_x32(tmem + lane_base + WCOL + 64 * sw, w);
           tmem_st_x32(tmem + lane_base + WCOL + 64 * sw + 32, w2);
+          tmem_st_wait(w);
+          tmem_st_keep(w2);
         }
-        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -447,7 +428,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
           const int c = ehalf * (BN2 / 2) + 32 * q;
           uint32_t accv[32];
           tmem_ld_x32(tmem + lane_base + ACC_COLS * buf + c, accv);
-          tmem_ld_wait();
+          tmem_ld_wait(accv);
           if (q == CH - 1 && sb == SUB - 1) {
             // every accumulator column of the tile is in registers: release the buffer(s)
             tc_fence_before();
@@ -505,6 +486,9 @@ __global__ void __launch_bounds__(THREADS2, 1)
       }
     }
   }
+  // stores into other GPUs' buffers (tensor-parallel output copies) are made visible at
+  // system scope by each storing thread before the kernel ends
+  if (!GROUPED && p.n_out_peer) __threadfence_system();
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its peer may still signal it
   if (warp == MMA_W) {

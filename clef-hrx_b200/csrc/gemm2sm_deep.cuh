@@ -272,20 +272,21 @@ __global__ void __launch_bounds__(DeepCfg<BN>::THREADS, 1)
         if (!(ok = waited)) break;
         tc_fence_after();
         // 8 words per 32-code group -> low nibbles then high nibbles (x16)
+        uint32_t o[2][32];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          uint32_t o[32];
 #pragma unroll
           for (int gq = 0; gq < 4; ++gq) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              o[8 * gq + q] = nib_lo16(w[16 * h + 4 * gq + q]);
-              o[8 * gq + 4 + q] = nib_hi16(w[16 * h + 4 * gq + q]);
+              o[h][8 * gq + q] = nib_lo16(w[16 * h + 4 * gq + q]);
+              o[h][8 * gq + 4 + q] = nib_hi16(w[16 * h + 4 * gq + q]);
             }
           }
-          tmem_st_x32(tmem + lane_base + WCOL + 64 * sw + 32 * h, o);
+          tmem_st_x32(tmem + lane_base + WCOL + 64 * sw + 32 * h, o[h]);
         }
-        tmem_st_wait();
+        tmem_st_wait(o[0]);
+        tmem_st_keep(o[1]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -330,7 +331,8 @@ __global__ void __launch_bounds__(DeepCfg<BN>::THREADS, 1)
         tc_fence_after();
         tmem_ld_x32(tmem + lane_base + ACC_COL + c0, accv[0]);
         tmem_ld_x32(tmem + lane_base + ACC_COL + c0 + 32, accv[1]);
-        tmem_ld_wait();
+        tmem_ld_wait(accv[0]);
+        tmem_ld_tie(accv[1]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -446,6 +448,9 @@ __global__ void __launch_bounds__(DeepCfg<BN>::THREADS, 1)
       named_barrier_sync(1, 32 * EPI);  // the staging buffer is free for the next tile
     }
   }
+  // stores into other GPUs' buffers (tensor-parallel output copies) are made visible at
+  // system scope by each storing thread before the kernel ends
+  if (!GROUPED && p.n_out_peer) __threadfence_system();
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its peer may still signal it
   if (warp == MMA_W) {

@@ -694,6 +694,10 @@ __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
     if (row_leader) reinterpret_cast<float *>(p.out + p.rows * words)[row] = scale;
   }
   cp_async_wait<0>();
+  // Code words stored into other ranks' buffers are made visible at system scope by the
+  // thread that stored them, before the kernel ends: the barrier kernel that follows raises
+  // the peers' flags from one thread, and its fence orders only what that thread observed.
+  if (TAB && p.n_code_dst) __threadfence_system();
 }
 
 namespace {

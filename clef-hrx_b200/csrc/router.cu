@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
     for (int c = 0; c < E; c += 32) {
       uint32_t v[32];
       tmem_ld_x32(tmem + lane_base + c, v);
-      tmem_ld_wait();
+      tmem_ld_wait(v);
       uint32_t packed[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {

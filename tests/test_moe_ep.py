@@ -151,10 +151,13 @@ def _weights(cq, experts, inter, hidden, seed):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world,experts,topk,tokens", [(2, 16, 4, 100), (4, 16, 4, 37), (4, 128, 8, 300)])
-def test_ep_simulated_ranks_match_single_gpu(cq, world, experts, topk, tokens):
+@pytest.mark.parametrize("world,experts,topk,tokens,hidden,inter", [
+    (2, 16, 4, 100, 512, 256), (4, 16, 4, 37, 512, 256), (4, 128, 8, 300, 512, 256),
+    (2, 128, 8, 1000, 2048, 768), (4, 64, 8, 333, 2048, 768), (2, 128, 8, 8192, 2048, 768)])
+def test_ep_simulated_ranks_match_single_gpu(cq, world, experts, topk, tokens, hidden, inter):
+    """Hidden 2048 takes the deep-ring kernel for the expert gate|up GEMM (K >= 2048), 512
+    the two-stage kernel."""
     from clefq.ep import CudaEpOps, shard_experts
-    hidden, inter = 512, 256
     gate, up, down = _weights(cq, experts, inter, hidden, 11)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(world * 100 + tokens)
@@ -198,7 +201,7 @@ def test_ep_simulated_ranks_match_single_gpu(cq, world, experts, topk, tokens):
 # ---------------------------------------------------------------------------------------
 # GPU, 2 processes over NCCL
 # ---------------------------------------------------------------------------------------
-def _nccl_worker(rank, world, port):
+def _nccl_worker(rank, world, port, hidden=512, inter=256):
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
     import clefq as cq
@@ -208,7 +211,7 @@ def _nccl_worker(rank, world, port):
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             device_id=torch.device("cuda", rank))
     try:
-        experts, topk, hidden, inter, tokens = 32, 8, 512, 256, 257 + 31 * rank
+        experts, topk, tokens = 32, 8, 257 + 31 * rank
         gate, up, down = _weights(cq, experts, inter, hidden, 5)
         shard = shard_experts(gate, up, down, experts, inter, hidden, rank, world)
         gen = torch.Generator(device="cuda")
@@ -225,21 +228,23 @@ def _nccl_worker(rank, world, port):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_ep_ranks_nccl(world):
+@pytest.mark.parametrize("hidden,inter", [(512, 256), (2048, 768)])
+def test_ep_ranks_nccl(world, hidden, inter):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.start_processes(_nccl_worker, args=(world, _free_port()), nprocs=world, join=True, start_method="spawn")
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), hidden, inter), nprocs=world, join=True,
+                       start_method="spawn")
 
 
 # ---------------------------------------------------------------------------------------
 # fused path: clefq_moe_ep_layer over a Comm (records and products stored into peers)
 # ---------------------------------------------------------------------------------------
 @pytest.mark.gpu
-@pytest.mark.parametrize("experts,topk,tokens", [(16, 4, 100), (128, 8, 300), (32, 8, 1)])
-def test_ep_fused_one_rank_matches_moe(cq, experts, topk, tokens):
+@pytest.mark.parametrize("experts,topk,tokens,hidden,inter", [
+    (16, 4, 100, 512, 256), (128, 8, 300, 512, 256), (32, 8, 1, 512, 256), (128, 8, 1000, 2048, 768)])
+def test_ep_fused_one_rank_matches_moe(cq, experts, topk, tokens, hidden, inter):
     from clefq.comm import Comm
     from clefq.ep import ep_layer_region_bytes, omni_moe_ep_fused, shard_experts
-    hidden, inter = 512, 256
     gate, up, down = _weights(cq, experts, inter, hidden, 17)
     shard = shard_experts(gate, up, down, experts, inter, hidden, 0, 1)
     gen = torch.Generator(device="cuda")
@@ -254,6 +259,39 @@ def test_ep_fused_one_rank_matches_moe(cq, experts, topk, tokens):
             assert torch.equal(routes, ref_routes)
             assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), f"call {rep}"
         cq.status()
+
+
+@pytest.mark.gpu
+def test_ep_fused_one_rank_full_size(cq):
+    """The fused layer at BASELINE configs[3] size on one rank (8192 tokens, hidden 2048, inter 768,
+    128 experts, top-8), with the benchmark's inputs: random int4 weight words, logits of
+    BF16 N(0, 1) rows through a BF16 N(0, 1) router weight.  Repeated calls and a receive
+    capacity above the routes present; every call bit-identical to clefq_moe."""
+    from clefq.comm import Comm
+    from clefq.ep import ep_layer_region_bytes, omni_moe_ep_fused, shard_experts
+    tokens, hidden, inter, experts, topk = 8192, 2048, 768, 128, 8
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2000)
+
+    def rand_weight(rows, cols):
+        codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (rows * cols // 8,), dtype=torch.int32, device="cuda",
+                              generator=gen)
+        scales = (torch.randn(rows, device="cuda", generator=gen).abs() * 0.02 / 7).float()
+        return cq.QuantizedWeight(codes, scales, rows, cols, cq.stride_for(cols), 4)
+    gate, up = rand_weight(experts * inter, hidden), rand_weight(experts * inter, hidden)
+    down = rand_weight(experts * hidden, inter)
+    x = torch.randn(tokens, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+    wr = torch.randn(experts, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+    logits = x @ wr.t()
+    ref = cq.omni_moe(x, logits, gate, up, down)
+    shard = shard_experts(gate, up, down, experts, inter, hidden, 0, 1)
+    for cap in (tokens * topk, 2 * tokens * topk):
+        with Comm(ep_layer_region_bytes(tokens, hidden, topk, 1, cap)) as comm:
+            for rep in range(3):
+                out, _ = omni_moe_ep_fused(x, logits, shard, comm, topk, recv_cap=cap)
+                bad = int((out.view(torch.int16) != ref.view(torch.int16)).sum())
+                assert bad == 0, f"capacity {cap}, call {rep}: {bad} outputs differ"
+    cq.status()
 
 
 @pytest.mark.gpu
@@ -280,7 +318,7 @@ def test_ep_fused_capacity_overflow_is_reported(cq):
     cq.status()
 
 
-def _nccl_fused_worker(rank, world, port):
+def _nccl_fused_worker(rank, world, port, hidden=512, inter=256):
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "clef-hrx_b200"))
     import clefq as cq
@@ -291,7 +329,7 @@ def _nccl_fused_worker(rank, world, port):
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             device_id=torch.device("cuda", rank))
     try:
-        experts, topk, hidden, inter = 32, 8, 512, 256
+        experts, topk = 32, 8
         most = 257 + 31 * (world - 1)
         cap = world * most * topk                   # the same on every rank
         gate, up, down = _weights(cq, experts, inter, hidden, 5)
@@ -314,7 +352,9 @@ def _nccl_fused_worker(rank, world, port):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_ep_fused_ranks(world):
+@pytest.mark.parametrize("hidden,inter", [(512, 256), (2048, 768)])
+def test_ep_fused_ranks(world, hidden, inter):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.start_processes(_nccl_fused_worker, args=(world, _free_port()), nprocs=world, join=True, start_method="spawn")
+    mp.start_processes(_nccl_fused_worker, args=(world, _free_port(), hidden, inter), nprocs=world, join=True,
+                       start_method="spawn")
