@@ -52,7 +52,7 @@ class Comm:
     @property
     def handle(self):
         if self._comm is None:
-            raise RuntimeError("TpComm is closed")
+            raise RuntimeError("Comm is closed")
         return self._comm
 
     def barrier(self):

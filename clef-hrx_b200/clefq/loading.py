@@ -150,7 +150,9 @@ def _json(obj) -> bytes:
 
 def packing_identity() -> str:
     """Identity of this build's packing: its layout tag and the sources that define the bytes
-    (a change of either misses every cached entry)."""
+    (a change of either misses every cached entry).  It hashes this build's own sources, so
+    cache files written by the reference (whose identity hashes its kernels) never match
+    here, and the reverse: the file format is shared, the entries are not."""
     here = Path(__file__).resolve().parent.parent / "csrc"
     h = hashlib.sha256(b"tiled256x64-to-rotated-codes128x32-v1\n")
     for name in ("prepare.cu", "cq_math.h", "cq_common.cuh", "load.cu"):
