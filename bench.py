@@ -178,6 +178,13 @@ def rand_weight_host(rng, rows, cols):
     return codes, scales, rows
 
 
+# GPU spin (~0.2 ms) queued after each step's L2 flush and before its start event: the host
+# has enqueued the whole step by the time the start event executes, so a step's time is its
+# device time and not the host's launch path (which the e2e line measures, host buffers
+# included).
+LEAD = 400_000
+
+
 def time_steps(fn, steps, flush, lead_cycles=0):
     """Device time of each step (CUDA events on the launching stream), L2 flushed before
     every step; returns per-step milliseconds.  lead_cycles > 0 queues a GPU spin after
@@ -265,7 +272,7 @@ def run_c1(clefq, gen, flush, args, world, rank, i8_peak):
         step()
     torch.cuda.synchronize()
     barrier(world)
-    times = time_steps(step, max(20, min(args.steps, 200)), flush, lead_cycles=400_000)
+    times = time_steps(step, max(20, min(args.steps, 200)), flush, lead_cycles=LEAD)
     ms = all_max(world, statistics.median(times))
     ops = 2.0 * m * n * k
     out = {"workload": "C1 single INT4 GEMM: 128 x 2048 BF16 rows packed, then 768 x 2048 int4 weight, F32 out",
@@ -343,6 +350,7 @@ def run_c3(clefq, gen, flush, args, world, rank, i8_peak):
     totals, atts = [], []
     for _ in range(max(3, min(args.steps, 10))):
         flush.fill_(1)
+        torch.cuda._sleep(LEAD)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         step(record=True)
@@ -437,7 +445,7 @@ def run_c5(clefq, gen, flush, args, world, rank, i8_peak):
     torch.cuda.synchronize()
     clefq.status()
     barrier(world)
-    times = time_steps(step, max(3, min(args.steps, 5)), flush)
+    times = time_steps(step, max(3, min(args.steps, 5)), flush, lead_cycles=LEAD)
     clefq.status()
     ms = all_max(world, statistics.median(times))
     if comm is not None:
@@ -504,7 +512,7 @@ def run_clefq(args, world, rank, local):
     clefq.status()
     barrier(world)
     torch.cuda.synchronize()
-    times = time_steps(step, args.steps, flush)
+    times = time_steps(step, args.steps, flush, lead_cycles=LEAD)
     torch.cuda.synchronize()
     barrier(world)
     clocks = sampler.stop()
@@ -533,7 +541,7 @@ def run_clefq(args, world, rank, local):
         clefq._call("clefq_gemm_s8", clefq._stream(), 4, clefq._ptr(hid.operand), INTER, clefq._ptr(hid.scales), M,
                     clefq._ptr(down.codes), clefq._ptr(down.scales), HIDDEN, INTER, None, 0, 0, clefq._ptr(out),
                     HIDDEN)
-    lead = 400_000   # ~0.2 ms of GPU spin ahead of each timed kernel
+    lead = LEAD
     for name, fn in (("gemm_gate_up", gemm_gu), ("gemm_down", gemm_down)):
         fn()
         ktimes[name] = statistics.median(time_steps(fn, reps, flush, lead))
@@ -645,7 +653,7 @@ def run_clefq(args, world, rank, local):
                 nstep()
             torch.cuda.synchronize()
             barrier(world)
-            nt = time_steps(nstep, max(5, min(args.steps, 30)), flush)
+            nt = time_steps(nstep, max(5, min(args.steps, 30)), flush, lead_cycles=LEAD)
             nccl_ms = all_max(world, sum(nt) / len(nt))
             mstep = lambda: omni_moe_ep_fused(mx, None, shard, ecomm, MOE_K, recv_cap=cap,  # noqa: E731
                                               workspace=ews, out=eout, router_weight=wr)
@@ -656,7 +664,7 @@ def run_clefq(args, world, rank, local):
         torch.cuda.synchronize()
         clefq.status()
         barrier(world)
-        mt = time_steps(mstep, max(5, min(args.steps, 30)), flush)
+        mt = time_steps(mstep, max(5, min(args.steps, 30)), flush, lead_cycles=LEAD)
         clefq.status()
         mms = all_max(world, sum(mt) / len(mt))
         if world > 1:
@@ -721,7 +729,7 @@ def run_clefq(args, world, rank, local):
             torch.cuda.synchronize()
             clefq.status()
             barrier(world)
-            tt = time_steps(step, max(5, min(args.steps, 30)), flush)
+            tt = time_steps(step, max(5, min(args.steps, 30)), flush, lead_cycles=LEAD)
             clefq.status()
             return all_max(world, sum(tt) / len(tt))
         fms = timed(lambda: mlp_tp_fused(tx, tshard, comm, workspace=tws, out=tout))

@@ -559,8 +559,10 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
     // int4 with at least 8 K stages: the deep-ring kernel, 256-token tiles for dense launches
     // and 192 for grouped ones (their tile lists are built for 192 rows).  Shorter K keeps
     // the two-stage kernel, whose double-buffered accumulators hide the tile hand-over that
-    // a few K stages cannot amortise.
-    const bool deep = p.bits == 4 && p.k / 256 >= CLEFQ_DEEP_MIN_KSTAGES;
+    // a few K stages cannot amortise.  A dense launch of one 256-token tile or less (C1: 128
+    // tokens, 3 pair tiles, 29.6 against 25.6 us per call) is latency-bound and keeps the
+    // two-stage kernel, whose set-up is lighter, unless it applies SwiGLU.
+    const bool deep = p.bits == 4 && p.k / 256 >= CLEFQ_DEEP_MIN_KSTAGES && (p.grouped || p.swiglu || p.m > 256);
 #else
     const bool deep = false;
 #endif
