@@ -272,8 +272,8 @@ CLEFQ_API int clefq_combine(void *stream, const void *values, const float *route
  * project_swiglu(gate, up, down, residual) (src/backbone.rs:880-894,
  * src/quantized.rs:406-439), bit-identical to those separate steps:
  *   prepare(x) -> gate, up projections -> SwiGLU -> prepare -> down projection (+ residual)
- * With hidden >= 2048 and inter % 256 == 0 the gate|up launch applies SwiGLU in its epilogue
- * and writes the hidden rows; otherwise SwiGLU is fused into their packing.
+ * With hidden >= 4096 and inter % 256 == 0 the gate|up launch applies SwiGLU in its epilogue
+ * and writes the hidden rows; otherwise SwiGLU is fused into their packing (same outputs).
  *   x BF16 [m][hidden]; gate/up tiled [inter][hidden] + scales; down tiled [hidden][inter]
  *   out BF16 [m][hidden]; residual BF16 [m][hidden] or NULL
  * workspace >= clefq_mlp_workspace_size(m, hidden, inter).

@@ -299,11 +299,12 @@ def test_gemm_swiglu_rejects_unsupported_shapes(cq):
             cq.project_swiglu_prepared(4, gdev, udev, a)
 
 
-@pytest.mark.parametrize("m,h,inter", [(200, 1024, 768), (300, 2048, 768), (1, 2048, 256), (257, 4096, 1280)])
+@pytest.mark.parametrize("m,h,inter", [(200, 1024, 768), (300, 2048, 768), (1, 4096, 256), (257, 4096, 1280),
+                                        (129, 4096, 512)])
 def test_mlp_block(cq, m, h, inter):
     """Dense SwiGLU MLP block through one C-ABI call, bit-exact to the oracle's separate
-    steps (prepare, gate, up, swiglu, prepare, down); hidden 1024 and inter 1280 take the
-    SwiGLU-in-packing route, the others SwiGLU in the gate|up epilogue."""
+    steps (prepare, gate, up, swiglu, prepare, down); hidden 4096 with inter a multiple of 256
+    takes SwiGLU in the gate|up epilogue, the others SwiGLU in the packing."""
     rng = np.random.default_rng(5 + m)
     ws = []
     for n, k in ((inter, h), (inter, h), (h, inter)):
