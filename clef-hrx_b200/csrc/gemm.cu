@@ -33,6 +33,14 @@
 #ifndef CLEFQ_GEMM_DEEP
 #define CLEFQ_GEMM_DEEP 1
 #endif
+// 1: grouped int4 launches of at most three K stages take the weight-resident kernel
+// (gemm2sm_wres.cuh); 0: the two-stage kernel, kept for comparison builds.
+#ifndef CLEFQ_GEMM_WRES
+#define CLEFQ_GEMM_WRES 1
+#endif
+#ifndef CLEFQ_WRES_SUBN
+#define CLEFQ_WRES_SUBN 192   // tokens per MMA of the weight-resident kernel: 192 or 96
+#endif
 
 namespace cq {
 
@@ -364,6 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 #include "gemm2sm.cuh"
 #include "gemm2sm_deep.cuh"
+#include "gemm2sm_wres.cuh"
 #ifndef CLEFQ_DEEP_MIN_KSTAGES
 #define CLEFQ_DEEP_MIN_KSTAGES 8   // fewest 256-wide K stages an int4 launch needs for the deep-ring kernel
 #endif
@@ -496,6 +505,13 @@ static cudaError_t launch_deep_2sm(int64_t pair_tiles, const CUtensorMap &t, con
                                                      pair_tiles, t, w0, w1, p, stream);
 }
 
+static cudaError_t launch_wres_2sm(int64_t pair_tiles, const CUtensorMap &t, const CUtensorMap &w0,
+                                   const CUtensorMap &w1, const GemmParams &p, cudaStream_t stream) {
+  return launch_pair_kernel<2000 + CLEFQ_WRES_SUBN>(two_sm_wres::gemm_i4_2sm_wres_kernel<CLEFQ_WRES_SUBN>,
+                                                    two_sm_wres::THREADS, two_sm_wres::WresCfg<CLEFQ_WRES_SUBN>::SMEM,
+                                                    pair_tiles, t, w0, w1, p, stream);
+}
+
 bool gemm_uses_pairs(const GemmParams &p) { return p.n_split % 2 == 0 && p.n % 256 == 0; }
 
 // Whether launch_gemm can apply the SwiGLU epilogue to a gate|up launch of n_each rows per
@@ -566,8 +582,11 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
 #else
     const bool deep = false;
 #endif
+    // grouped int4 with at most three K stages (the MoE down projection, K = 768): the
+    // weight-resident kernel over the 192-row tile list
+    const bool wres = CLEFQ_GEMM_WRES && p.grouped && p.bits == 4 && !p.swiglu && p.k / 256 <= two_sm_wres::MAX_KST;
     const int deep_bn = p.grouped ? 192 : 256;
-    const int half = deep ? deep_bn / 2 : two_sm::HALF;
+    const int half = wres ? two_sm_wres::WresCfg<CLEFQ_WRES_SUBN>::SH : (deep ? deep_bn / 2 : two_sm::HALF);
     // token operand as 3D: x = 128 bytes of a K slice, y = rows (pitch a_ld), z = K slices
     cuuint64_t d3[3] = {128, (cuuint64_t)p.a_rows, (cuuint64_t)(p.k / 128)};
     cuuint64_t s3[2] = {(cuuint64_t)p.a_ld, 128};
@@ -595,6 +614,10 @@ int launch_gemm(const GemmParams &p0, cudaStream_t stream) {
     }
     const int64_t pair_tiles = tiles_m * (p.n / two_sm::BMP);
     cudaError_t e;
+    if (wres) {
+      e = launch_wres_2sm(pair_tiles, tmap, wmap0, wmap1, p, stream);
+      return e == cudaSuccess ? 0 : CLEFQ_ERR_CUDA;
+    }
     if (deep) {
       if (p.grouped) {
         e = launch_deep_2sm<true, 192>(pair_tiles, tmap, wmap0, wmap1, p, stream);

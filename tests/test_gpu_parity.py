@@ -410,10 +410,12 @@ def _expert_weights(rng, experts, n, k):
 
 
 @pytest.mark.parametrize("tokens,skewed", [(1, False), (37, False), (300, True), (1000, False)])
-@pytest.mark.parametrize("routed,k,n", [(False, 512, 256), (True, 256, 512), (False, 256, 384), (True, 256, 384)])
+@pytest.mark.parametrize("routed,k,n", [(False, 512, 256), (True, 256, 512), (False, 256, 384), (True, 256, 384),
+                                        (True, 768, 512), (False, 768, 256)])
 def test_expert_matches_oracle(cq, tokens, skewed, routed, k, n):
     """Grouped INT4 experts, bit-exact (src/benchmarking/omni.rs:176-345 fixtures); n=384
-    runs the one-CTA kernel, multiples of 256 the CTA-pair kernel."""
+    runs the one-CTA kernel, multiples of 256 the CTA-pair kernels (K <= 768: the
+    weight-resident kernel, whose units of one expert's tiles end at ragged expert tails)."""
     from tests.golden.make_golden import expert_routes
     rng = np.random.default_rng(tokens)
     experts, topk = 128, 8
