@@ -280,6 +280,14 @@ CQ_DEV void tmem_ld_tie(uint32_t (&v)[32]) {
                : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream serialization
+// may start while the previous kernel of its stream still runs: pdl_wait() returns once that
+// kernel has completed and its memory is visible, so nothing that kernel writes (or reads and
+// this kernel overwrites) may be touched before it.  pdl_trigger() lets the next such kernel
+// of the stream be scheduled; it waits in its own pdl_wait() all the same.
+CQ_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+CQ_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 CQ_DEV uint4 ldg_nc_v4(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 
 // --- clusters and 2-SM (cta_group::2) forms --------------------------------------------

@@ -38,6 +38,11 @@
 #ifndef CLEFQ_GEMM_WRES
 #define CLEFQ_GEMM_WRES 1
 #endif
+// 1: the pair GEMMs and the packing kernels are launched with programmatic stream
+// serialization (each waits in-kernel for the previous kernel, griddepcontrol).
+#ifndef CLEFQ_PDL
+#define CLEFQ_PDL 1
+#endif
 #ifndef CLEFQ_WRES_SUBN
 #define CLEFQ_WRES_SUBN 192   // tokens per MMA of the weight-resident kernel: 192 or 96
 #endif
@@ -465,7 +470,7 @@ static cudaError_t launch_pair_kernel(PairKernel kern, int threads, int smem, in
   std::atomic<int> &slot = (dev >= 0 && dev < 64) ? max_clusters_dev[dev] : scratch;
   int max_clusters = slot.load(std::memory_order_acquire);
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -486,6 +491,10 @@ static cudaError_t launch_pair_kernel(PairKernel kern, int threads, int smem, in
   }
   const int64_t clusters = pair_tiles < max_clusters ? pair_tiles : max_clusters;
   cfg.gridDim = dim3((unsigned)(2 * clusters));
+  // programmatic dependent launch: the pair kernels wait for the previous kernel in-kernel
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = CLEFQ_PDL;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, t, w0, w1, p);
 }
 

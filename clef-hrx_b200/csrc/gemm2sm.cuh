@@ -164,6 +164,11 @@ __global__ void __launch_bounds__(THREADS2, 1)
   const uint32_t rank = cluster_ctarank();
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
 
+  // grouped: the tile list is the previous kernel's output
+  if (GROUPED) {
+    pdl_wait();
+    pdl_trigger();
+  }
   TileMap2 tm;
   tm.n_pairs = p.n / BMP;
   tm.span = SUB * BN2;
@@ -199,6 +204,12 @@ __global__ void __launch_bounds__(THREADS2, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // dense: the prologue above touches no global memory; tokens, scales, residual and
+  // output wait for the previous kernel
+  if (!GROUPED) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   // Output/weight tile of this CTA for pair tile np: 128-row tile 2*np + rank.
   auto weight_tile = [&](int np, int expert, int &which, int &w_row_tile) {

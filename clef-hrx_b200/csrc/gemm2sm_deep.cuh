@@ -102,6 +102,11 @@ __global__ void __launch_bounds__(DeepCfg<BN>::THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
 
+  // grouped: the tile list is the previous kernel's output
+  if (GROUPED) {
+    pdl_wait();
+    pdl_trigger();
+  }
   TileMap2 tm;
   tm.n_pairs = p.n / BMP;
   tm.span = BN;
@@ -135,6 +140,12 @@ __global__ void __launch_bounds__(DeepCfg<BN>::THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // dense: the prologue above touches no global memory; tokens, scales, residual and
+  // output wait for the previous kernel
+  if (!GROUPED) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   auto weight_tile = [&](int np, int expert, int &which, int &w_row_tile) {
     const int nt = 2 * np + (int)rank;

@@ -120,6 +120,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
 
+  // the tile list is the previous kernel's output
+  pdl_wait();
+  pdl_trigger();
   Walk wk;
   wk.n_mt = p.tile_list[0];
   const int n_pairs = p.n / BMP;

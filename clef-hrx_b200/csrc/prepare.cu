@@ -22,6 +22,12 @@
 #include "cq_common.cuh"
 #include "clefq_internal.h"
 
+// 1: the packing kernels are launched with programmatic stream serialization (each waits
+// in-kernel for the previous kernel, griddepcontrol).
+#ifndef CLEFQ_PDL_PREPARE
+#define CLEFQ_PDL_PREPARE 1
+#endif
+
 namespace cq {
 
 enum { MODE_PLAIN = 0, MODE_SWIGLU = 1, MODE_ATTN_GATE = 2, MODE_NORM = 3, MODE_NORM_STORE = 4 };
@@ -220,6 +226,9 @@ CQ_DEV void stage_groups(const PrepareArgs &p, uint32_t stage_base, int64_t row,
 // buffered by iteration parity, so one barrier per phase is enough.
 template <int CH, int KIND>
 __global__ void __launch_bounds__(512, min_blocks_for(CH, KIND)) prepare_kernel(PrepareArgs p) {
+  // launched with programmatic stream serialization: the input is the previous kernel's output
+  pdl_wait();
+  pdl_trigger();
   constexpr bool FAST = KIND != KIND_GENERAL;
   constexpr bool TAB = KIND == KIND_SILU_TABLE;
   constexpr int STG = stages_for(CH, KIND);
@@ -489,6 +498,9 @@ constexpr int kPackRedBytes = 2 * 64 * 4;  // [2][64] team maxima (16 warps x 4 
 // CTA; p.stages cp.async stages per thread of NS x NOP x 64 bytes each.
 template <int NS, bool TAB>
 __global__ void __launch_bounds__(512, 1) pack_kernel(PrepareArgs p) {
+  // launched with programmatic stream serialization: the input is the previous kernel's output
+  pdl_wait();
+  pdl_trigger();
   constexpr int NOP = TAB ? 2 : 1;
   extern __shared__ __align__(16) uint8_t smem[];
   const uint16_t *tab = reinterpret_cast<const uint16_t *>(smem);
@@ -738,6 +750,23 @@ int resident_ctas(int threads, size_t smem) {
   return n;
 }
 
+// Launch with programmatic stream serialization (the kernels wait for the previous kernel
+// in-kernel, pdl_wait), so their start overlaps the previous kernel's last blocks.
+void launch_pdl(void (*kern)(PrepareArgs), unsigned grid, int threads, size_t smem, cudaStream_t stream,
+                const PrepareArgs &a) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = CLEFQ_PDL_PREPARE;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, a);
+}
+
 template <int CH, int KIND>
 void launch_instance(const PrepareArgs &a, int threads, size_t smem0, int64_t nblk, cudaStream_t stream) {
   constexpr int STG = stages_for(CH, KIND);
@@ -745,7 +774,7 @@ void launch_instance(const PrepareArgs &a, int threads, size_t smem0, int64_t nb
   const int per_sm = resident_ctas<CH, KIND>(threads, smem);
   int64_t grid = (int64_t)device_sms() * per_sm;
   if (grid > nblk) grid = nblk;
-  prepare_kernel<CH, KIND><<<(unsigned)grid, threads, smem, stream>>>(a);
+  launch_pdl(prepare_kernel<CH, KIND>, (unsigned)grid, threads, smem, stream, a);
 }
 
 template <int KIND>
@@ -778,7 +807,7 @@ void launch_pack(const PrepareArgs &a, int threads, size_t smem, int64_t nblk, c
   }
   int64_t grid = device_sms();
   if (grid > nblk) grid = nblk;
-  pack_kernel<NS, TAB><<<(unsigned)grid, threads, smem, stream>>>(a);
+  launch_pdl(pack_kernel<NS, TAB>, (unsigned)grid, threads, smem, stream, a);
 }
 
 // GEMM-input packing: int4 codes with the s8 operand, 16-byte aligned rows, no pre-op or
